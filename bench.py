@@ -1,0 +1,493 @@
+"""Benchmark of the B200 DeviceRadixSort hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl rccl_b200|reference]
+
+One step is one sort of the workload's whole input.  `value` is device-timed
+sorted keys/s with the input resident in HBM (CUDA events around each sort on
+the sort's stream; the untimed restore copy of the input happens between
+steps).  `e2e` is the same metric through the public rccl-thrust style API
+(thrust.with_values(...).sort()) with the input copied from pinned host memory
+and the sorted keys and values copied back inside the timed region.
+
+Workloads are seeded synthetic inputs with the reference benchmark shapes
+(numpy PCG64):
+  1: 2^20 u32 keys, uniform, ascending keys-only                (seed 1)
+  2: 2^28 u64 keys uniform over 64 bits + u32 values = index,
+     stable ascending pairs (default; the north-star pair config)  (seed 2)
+  3: 2^28 f32 keys ~ N(0, 1e3) with +-0 / +-inf / NaN, descending (seed 3)
+  4: 2^30 u32 keys, 90% Zipf(1.1) over 2^20 values + 10% constant (seeds 4, 5)
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "sorted keys/s (device-timed)"
+UNIT = "keys/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ---------------------------------------------------------------------------
+# Workloads
+# ---------------------------------------------------------------------------
+class Workload:
+    def __init__(self, config: int, n_override: int | None = None):
+        self.config = config
+        if config == 1:
+            self.n, self.key, self.value, self.desc = 1 << 20, np.uint32, None, False
+            self.name = "keys-only u32 ascending, uniform"
+        elif config == 2:
+            self.n, self.key, self.value, self.desc = 1 << 28, np.uint64, np.uint32, False
+            self.name = "stable pairs u64 keys / u32 values ascending, uniform"
+        elif config == 3:
+            self.n, self.key, self.value, self.desc = 1 << 28, np.float32, None, True
+            self.name = "keys-only f32 descending, N(0,1e3) with +-0/+-inf/NaN"
+        elif config == 4:
+            self.n, self.key, self.value, self.desc = 1 << 30, np.uint32, None, False
+            self.name = "keys-only u32 ascending, 90% Zipf(1.1) over 2^20 + 10% constant"
+        else:
+            raise SystemExit(f"unknown config {config}")
+        if n_override:
+            self.n = n_override
+        self.kb = np.dtype(self.key).itemsize
+        self.vb = np.dtype(self.value).itemsize if self.value is not None else 0
+        self.passes = self.kb  # 8-bit digits over the full key width
+
+    @property
+    def bytes_per_sort(self) -> int:
+        # one histogram read + per pass read and write of keys and values
+        return self.n * self.kb + self.passes * 2 * self.n * (self.kb + self.vb)
+
+    @property
+    def bytes_per_pass(self) -> int:
+        return 2 * self.n * (self.kb + self.vb)
+
+    def generate(self, n: int | None = None, offset: int = 0):
+        """Host arrays (keys, values) of this workload (`n` items from `offset`)."""
+        n = self.n if n is None else n
+        c = self.config
+        if c == 1:
+            keys = np.random.default_rng(1).integers(0, 2**32, self.n, dtype=np.uint64)
+            keys = keys[offset:offset + n].astype(np.uint32)
+        elif c == 2:
+            rng = np.random.default_rng(2)
+            if offset:
+                rng.integers(0, 2**64, offset, dtype=np.uint64)
+            keys = rng.integers(0, 2**64, n, dtype=np.uint64)
+        elif c == 3:
+            keys = gen_f32_specials(np.random.default_rng(3 + offset), n)
+        else:
+            keys = gen_zipf(n, seed_offset=offset)
+        values = None
+        if self.value is not None:
+            values = np.arange(offset, offset + n, dtype=np.uint64).astype(self.value)
+        return keys, values
+
+
+def gen_f32_specials(rng, n):
+    x = rng.normal(0.0, 1e3, n).astype(np.float32)
+    n_zero, n_inf, n_nan = n // 1000, n // 10000, n // 10000
+    pos = rng.choice(n, n_zero + n_inf + n_nan, replace=False)
+    z, i, q = pos[:n_zero], pos[n_zero:n_zero + n_inf], pos[n_zero + n_inf:]
+    bits = x.view(np.uint32)
+    sign = rng.integers(0, 2, pos.size).astype(np.uint32) << 31
+    bits[z] = sign[:n_zero]
+    bits[i] = 0x7F800000 | sign[n_zero:n_zero + n_inf]
+    payload = rng.integers(1, 1 << 22, n_nan).astype(np.uint32)
+    bits[q] = 0x7FC00000 | payload | sign[n_zero + n_inf:]
+    return x
+
+
+def gen_zipf(n, seed_offset=0):
+    rng = np.random.default_rng(4 + seed_offset)
+    ranks = np.arange(1, (1 << 20) + 1, dtype=np.float64)
+    cdf = np.cumsum(ranks ** -1.1)
+    cdf /= cdf[-1]
+    mapping = np.random.default_rng(5).choice(2**32, 1 << 20, replace=False).astype(np.uint32)
+    n_zipf = n * 9 // 10
+    u = rng.random(n_zipf)
+    keys = np.empty(n, np.uint32)
+    keys[:n_zipf] = mapping[np.searchsorted(cdf, u)]
+    keys[n_zipf:] = np.uint32(rng.integers(0, 2**32))
+    rng.shuffle(keys)
+    return keys
+
+
+# ---------------------------------------------------------------------------
+# Helpers
+# ---------------------------------------------------------------------------
+def measured_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            return float(json.load(fh)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic(workload: Workload):
+    """DRAM bytes per onesweep launch from the committed ncu summary, scaled
+    from the captured size to this workload's size (traffic grows with n)."""
+    path = os.path.join(ROOT, "profiles", "traffic.txt")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        f = dict(kv.split("=", 1) for kv in line.split() if "=" in kv)
+        if f.get("config") == str(workload.config) and f.get("kernel") == "onesweep":
+            return float(f["dram_bytes_per_launch"]) * workload.n / float(f["n"])
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.reader.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[4:8]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def order_image(keys: np.ndarray, descending: bool) -> np.ndarray:
+    """Unsigned image whose ascending order is the sort order (radix.rs:75-235
+    transforms with the float zero fold)."""
+    w = keys.dtype.itemsize * 8
+    u = keys.view(np.uint32 if w == 32 else np.uint64)
+    sign = (np.uint32 if w == 32 else np.uint64)(1 << (w - 1))
+    if keys.dtype.kind == "f":
+        neg = (u & sign) != 0
+        o = np.where(neg, ~u, u ^ sign)
+    elif keys.dtype.kind == "i":
+        o = u ^ sign
+    else:
+        o = u.copy()
+    if descending:
+        o = ~o
+    if keys.dtype.kind == "f":
+        o = np.where(o == sign - 1, sign, o)
+    return o
+
+
+def cpu_baseline(workload: Workload, budget_s: float = 12.0):
+    """The oracle port (stable LSD radix restatement) on all host cores over a
+    bounded sample of the workload."""
+    from oracle import pyoracle
+    threads = os.cpu_count() or 1
+    sample = min(workload.n, 1 << 24)
+    keys, values = workload.generate(sample)
+    rates = []
+    t_end = time.perf_counter() + budget_s
+    while len(rates) < 5 and (len(rates) < 1 or time.perf_counter() < t_end):
+        t0 = time.perf_counter()
+        pyoracle.radix_sort(keys, values, workload.desc, threads=threads)
+        rates.append(sample / (time.perf_counter() - t0))
+    return {"value": statistics.median(rates), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"first {sample} items of the workload, {len(rates)} timed sorts, "
+                      f"median; oracle stable LSD radix on {threads} host threads"}
+
+
+# ---------------------------------------------------------------------------
+# Reference arm: the reference's CPU restatement (oracle port), rank 0 only
+# ---------------------------------------------------------------------------
+def run_reference(args, workload: Workload, rank: int):
+    if rank != 0:
+        return
+    from oracle import pyoracle
+    threads = os.cpu_count() or 1
+    sample = min(workload.n, 1 << 24)
+    keys, values = workload.generate(sample)
+    for _ in range(args.warmup):
+        pyoracle.radix_sort(keys, values, workload.desc, threads=threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        pyoracle.radix_sort(keys, values, workload.desc, threads=threads)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = sample * args.steps / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": np.dtype(workload.key).name,
+        "data": "synthetic", "config": config_dict(args, workload, sample_n=sample),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"first {sample} items of the workload per step"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(args, workload: Workload, sample_n=None):
+    d = {"workload": f"config {workload.config}: {workload.name}", "n": workload.n,
+         "key": np.dtype(workload.key).name,
+         "value": np.dtype(workload.value).name if workload.value is not None else None,
+         "order": "descending" if workload.desc else "ascending", "stable": True,
+         "per_gpu_n": workload.n, "parallelism": f"sample-sort x{args.gpus}" if args.gpus > 1
+         else "single GPU",
+         "l2": "input larger than the 126 MB L2; untimed restore copy between steps"}
+    if sample_n is not None:
+        d["sample_n"] = sample_n
+    return d
+
+
+# ---------------------------------------------------------------------------
+# Single GPU
+# ---------------------------------------------------------------------------
+def run_single(args, workload: Workload):
+    import torch
+    from rccl_b200 import _lib, cub, thrust
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    launch = cub.Program.load(dev).on()
+    stream = launch.stream
+    keys_h, values_h = workload.generate()
+    kd = torch.from_numpy(keys_h[:0]).dtype
+    src_k = torch.from_numpy(keys_h).to(dev)
+    keys = torch.empty_like(src_k)
+    if values_h is not None:
+        src_v = torch.from_numpy(values_h).to(dev)
+        values = torch.empty_like(src_v)
+        ws = cub.device_radix_sort_pairs_workspace(launch, kd, src_v.dtype, workload.n)
+    else:
+        src_v = values = None
+        ws = cub.device_radix_sort_workspace(launch, kd, workload.n)
+    controls = ws.controls
+
+    def restore():
+        keys.copy_(src_k)
+        if values is not None:
+            values.copy_(src_v)
+
+    def sort():
+        if values is None:
+            (cub.device_radix_sort_keys_descending if workload.desc
+             else cub.device_radix_sort_keys)(launch, keys, ws)
+        else:
+            (cub.device_radix_sort_pairs_descending if workload.desc
+             else cub.device_radix_sort_pairs)(launch, keys, values, ws)
+
+    for _ in range(args.warmup):
+        restore()
+        sort()
+    cub.check_device_status(launch, controls)
+    torch.cuda.synchronize()
+
+    L = _lib.lib()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    L.rsort_launch_count_reset()
+    L.rsort_profile_read(None, None, 0)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        torch.cuda.synchronize()
+        for i in range(args.steps):
+            restore()
+            L.rsort_profile_enable(1)
+            starts[i].record(stream)
+            sort()
+            stops[i].record(stream)
+            L.rsort_profile_enable(0)
+        torch.cuda.synchronize()
+    launches = int(L.rsort_launch_count())
+    cub.check_device_status(launch, controls)
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, stops)]
+    total_ms = sum(step_ms)
+
+    import ctypes
+    cap = 64 * args.steps
+    kid = (ctypes.c_int32 * cap)()
+    kms = (ctypes.c_float * cap)()
+    nrec = L.rsort_profile_read(kid, kms, cap)
+    per_kernel = {}
+    for i in range(min(nrec, cap)):
+        per_kernel.setdefault(_lib.KERNEL_NAMES.get(kid[i], str(kid[i])), []).append(kms[i])
+
+    # Size-independent properties of the timed output: non-decreasing order
+    # image, and for pairs the values (= input index) form the permutation
+    # that maps the input onto the output, ascending within equal keys.
+    out_k = keys.cpu().numpy()
+    img = order_image(out_k, workload.desc)
+    ok = bool(np.all(img[1:] >= img[:-1]))
+    if values is not None:
+        out_v = values.cpu().numpy().astype(np.int64)
+        ok = ok and bool(np.array_equal(keys_h[out_v], out_k))
+        ties = img[1:] == img[:-1]
+        ok = ok and bool(np.all(out_v[1:][ties] > out_v[:-1][ties]))
+
+    peak, peak_kind = measured_peak()
+    osw = per_kernel.get("onesweep", [])
+    roofline = None
+    if osw:
+        avg_s = statistics.mean(osw) / 1e3
+        achieved = workload.bytes_per_pass / avg_s / 1e9
+        traffic = profiled_traffic(workload)
+        roofline = {"bound": "hbm", "kernel": "onesweep", "achieved": achieved, "peak": peak,
+                    "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
+                    "traffic": traffic, "algorithmic_bytes_per_launch": workload.bytes_per_pass,
+                    "avg_launch_ms": avg_s * 1e3,
+                    "sort_achieved": workload.bytes_per_sort / (total_ms / args.steps / 1e3) / 1e9,
+                    "sort_frac": workload.bytes_per_sort / (total_ms / args.steps / 1e3) / 1e9
+                    / peak}
+    kernel_ms = {k: {"launches": len(v), "total_ms": sum(v), "avg_ms": statistics.mean(v)}
+                 for k, v in per_kernel.items()}
+
+    e2e = run_e2e(args, workload, keys_h, values_h, dev)
+    del src_k, keys, src_v, values, ws
+    torch.cuda.empty_cache()
+
+    value = workload.n * args.steps / (total_ms / 1e3)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": np.dtype(workload.key).name,
+        "data": "synthetic (numpy PCG64, seeded)", "config": config_dict(args, workload),
+        "roofline": roofline, "e2e": e2e, "gpu_launches": launches,
+        "kernels": kernel_ms, "clocks": clocks.summary(), "output_checked": ok,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(workload)
+    print(json.dumps(line), flush=True)
+
+
+def run_e2e(args, workload: Workload, keys_h, values_h, dev):
+    """Public API end to end: pinned H2D, thrust-style sort, D2H of the result."""
+    import torch
+    from rccl_b200 import thrust
+
+    execution = thrust.Program.load(dev).par()
+    stream = execution.stream
+    hk = torch.from_numpy(keys_h).pin_memory()
+    ok_ = torch.empty_like(hk).pin_memory()
+    dk = torch.empty(hk.shape, dtype=hk.dtype, device=dev)
+    hv = ov = dv = None
+    if values_h is not None:
+        hv = torch.from_numpy(values_h).pin_memory()
+        ov = torch.empty_like(hv).pin_memory()
+        dv = torch.empty(hv.shape, dtype=hv.dtype, device=dev)
+    h2d = hk.numel() * hk.element_size() + (hv.numel() * hv.element_size() if hv is not None else 0)
+
+    def step():
+        with torch.cuda.stream(stream):
+            dk.copy_(hk, non_blocking=True)
+            if dv is not None:
+                dv.copy_(hv, non_blocking=True)
+        if workload.desc:
+            # rccl-thrust has no comparator-free descending sort; use the CUB
+            # descending entry point through the same temporary-allocating path.
+            from rccl_b200 import cub
+            launch = execution.launch
+            ws = cub.device_radix_sort_workspace(launch, dk.dtype, dk.numel())
+            cub.device_radix_sort_keys_descending(launch, dk, ws)
+            stream.synchronize()
+        elif dv is None:
+            thrust.sort(execution, dk)
+        else:
+            thrust.with_values(dk, dv).sort(execution)
+        with torch.cuda.stream(stream):
+            ok_.copy_(dk, non_blocking=True)
+            if dv is not None:
+                ov.copy_(dv, non_blocking=True)
+
+    steps = max(1, min(args.steps, 5))
+    for _ in range(min(args.warmup, 2)):
+        step()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / steps
+    return {"value": workload.n / (ms / 1e3), "unit": UNIT, "ms_per_step": ms,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": h2d, "steps": steps,
+            "api": "rccl_b200.thrust with_values().sort() (temporary allocation + sync per call)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--n", type=int, default=None, help="override the workload size")
+    ap.add_argument("--impl", default="rccl_b200", choices=["rccl_b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    workload = Workload(args.config, args.n)
+    if args.impl == "reference":
+        run_reference(args, workload, rank)
+        return
+    if world > 1 or args.gpus > 1:
+        from rccl_b200 import dist_bench
+        dist_bench.run(args, workload)
+        return
+    run_single(args, workload)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,164 @@
+/*
+ * rsort_b200 -- B200 (sm_100a) DeviceRadixSort behind a C ABI.
+ *
+ * This is the drop-in seam for rccl-cub's radix pass control.  In the
+ * reference the pass schedule lives in Rust (rccl-cub/src/radix.rs:425-876)
+ * and calls the kernel traits RadixKernel / RadixKeysKernel /
+ * RadixPairsKernel (rccl-cub/src/radix.rs:205-362).  Here one C call owns the
+ * whole schedule for one sort, so the Rust side replaces the bodies of
+ * device_radix_sort_keys_buffer / device_radix_sort_pairs_buffer with a single
+ * call each (see INTEGRATION.md for the binding).
+ *
+ * Conventions (rccl-cub semantics kept):
+ *  - All device memory is owned by the caller (keys, values, scratch and the
+ *    three control regions).  The single-GPU entry points never allocate.
+ *  - Calls are asynchronous on `stream`; nothing synchronizes the stream
+ *    (rccl-cub/src/radix.rs:425-554 never synchronizes either).
+ *  - Validation errors leave every buffer and the selector unchanged.
+ *  - `n == 0` or an empty bit window returns RSORT_OK with no launch and no
+ *    selector change (rccl-cub/src/radix.rs:467-469).
+ *  - The reference's "Policy800 one-portion maximum" length limit
+ *    (rccl-cub/src/radix.rs:377-384) is deliberately lifted: offsets are 64-bit.
+ */
+#ifndef RSORT_B200_H
+#define RSORT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same binary layout as cudaStream_t. */
+typedef struct CUstream_st *rsort_stream_t;
+
+/* The six RadixKey implementations (rccl-cub/src/radix.rs:114-173). */
+typedef enum {
+    RSORT_U32 = 0,
+    RSORT_I32 = 1,
+    RSORT_F32 = 2,
+    RSORT_U64 = 3,
+    RSORT_I64 = 4,
+    RSORT_F64 = 5
+} rsort_key_t;
+
+/* Maps 1:1 onto rccl_cub::DeviceAlgorithmError (rccl-cub/src/error.rs:3-25). */
+typedef enum {
+    RSORT_OK = 0,
+    RSORT_INVALID_BIT_RANGE = 1,   /* InvalidBitRange { begin, end, key_bits } */
+    RSORT_LENGTH_MISMATCH = 2,     /* LengthMismatch { role, expected, actual } */
+    RSORT_WORKSPACE_TOO_SMALL = 3, /* WorkspaceTooSmall { role, required, actual } */
+    RSORT_UNSUPPORTED_TARGET = 4,  /* UnsupportedTarget: device is not sm_100 */
+    RSORT_SIZE_OVERFLOW = 5,       /* SizeOverflow */
+    RSORT_CUDA_ERROR = 6,          /* Driver / Launch */
+    RSORT_TIMEOUT = 7,             /* a bounded device wait gave up (no reference variant) */
+    RSORT_BAD_ARGUMENT = 8         /* unsupported layout, null pointer, misalignment */
+} rsort_status;
+
+/* Element counts of the three control regions, in the element types of
+ * rccl-cub's DeviceRadixSortBufferWorkspace (bins: u64, lookback: i32,
+ * counters: i32; rccl-cub/src/workspace.rs:68-106).  Zero for inputs the
+ * single-tile route sorts, as in radix_control_lengths (workspace.rs:96-106). */
+typedef struct {
+    size_t bins;     /* uint64_t elements */
+    size_t lookback; /* int32_t elements; the region must be 16-byte aligned */
+    size_t counters; /* int32_t elements */
+} rsort_controls;
+
+/* Details of the last non-OK status returned on the calling host thread
+ * (the payload of the matching DeviceAlgorithmError variant). */
+typedef struct {
+    rsort_status status;
+    const char *role;  /* static string, e.g. "radix lookback" */
+    size_t expected;   /* expected / required length */
+    size_t actual;
+    unsigned begin_bit, end_bit, key_bits; /* InvalidBitRange payload */
+} rsort_error_info;
+
+/* Control-region sizes for `n` items (replaces
+ * rccl-cub/src/workspace.rs:68-106 device_radix_sort_*workspace_counts).
+ * value_bytes = 0 for keys-only; otherwise 1, 2, 4, 8 or 16. */
+rsort_status rsort_controls_query(rsort_key_t key, size_t value_bytes, size_t n,
+                                  rsort_controls *out);
+
+/* Keys-only DoubleBuffer sort over bits [begin_bit, end_bit)
+ * (replaces rccl-cub/src/radix.rs:425-554 device_radix_sort_keys_buffer and
+ * the eight-kernel RadixKeysKernel seam it drives).  *current_is_first is the
+ * DoubleBuffer selector: read on entry, updated on success exactly as the
+ * reference's swaps update it. */
+rsort_status rsort_keys_buffer(rsort_key_t key, int descending, void *d_first, void *d_second,
+                               size_t n, unsigned begin_bit, unsigned end_bit,
+                               int *current_is_first, uint64_t *bins, size_t nbins,
+                               int32_t *lookback, size_t nlookback, int32_t *counters,
+                               size_t ncounters, rsort_stream_t stream);
+
+/* Key/value DoubleBuffer sort (replaces rccl-cub/src/radix.rs:625-778
+ * device_radix_sort_pairs_buffer and the RadixPairsKernel seam).  Values are
+ * opaque value_bytes-wide items (1, 2, 4, 8 or 16 bytes) moved stably with
+ * their keys. */
+rsort_status rsort_pairs_buffer(rsort_key_t key, int descending, void *d_keys_first,
+                                void *d_keys_second, void *d_values_first, void *d_values_second,
+                                size_t value_bytes, size_t n, unsigned begin_bit, unsigned end_bit,
+                                int *current_is_first, uint64_t *bins, size_t nbins,
+                                int32_t *lookback, size_t nlookback, int32_t *counters,
+                                size_t ncounters, rsort_stream_t stream);
+
+/* In-place full-width keys sort with caller scratch (replaces
+ * rccl-cub/src/radix.rs:556-623 device_radix_sort_keys; scratch must hold n
+ * keys).  The sorted keys always end in d_keys. */
+rsort_status rsort_keys(rsort_key_t key, int descending, void *d_keys, void *d_scratch,
+                        size_t nscratch, size_t n, uint64_t *bins, size_t nbins, int32_t *lookback,
+                        size_t nlookback, int32_t *counters, size_t ncounters,
+                        rsort_stream_t stream);
+
+/* In-place full-width pairs sort (replaces rccl-cub/src/radix.rs:780-876
+ * device_radix_sort_pairs). */
+rsort_status rsort_pairs(rsort_key_t key, int descending, void *d_keys, void *d_values,
+                         size_t value_bytes, void *d_scratch_keys, size_t nscratch_keys,
+                         void *d_scratch_values, size_t nscratch_values, size_t n, uint64_t *bins,
+                         size_t nbins, int32_t *lookback, size_t nlookback, int32_t *counters,
+                         size_t ncounters, rsort_stream_t stream);
+
+/* Synchronizes `stream` and reports whether a bounded device wait of an
+ * earlier sort using these counters gave up (RSORT_TIMEOUT), then clears the
+ * flag.  The flag is sticky across sorts; a fresh counters region must be
+ * zeroed once (as rccl-cub's workspace constructors zero theirs,
+ * rccl-cub/src/workspace.rs:114-119).  No reference counterpart: the reference's look-back spin is
+ * unbounded (rccl-cub/src/ordering_backend/radix.rs:991-1011). */
+rsort_status rsort_check_device_status(int32_t *counters, size_t ncounters,
+                                       rsort_stream_t stream);
+
+/* Single-tile extent used for routing: identical to the reference's Policy800
+ * threshold (rccl-cub/src/workspace.rs:43-66). */
+size_t rsort_single_tile_items(rsort_key_t key, size_t value_bytes);
+
+/* Number of DoubleBuffer selector flips a successful call performs. */
+int rsort_selector_flips(rsort_key_t key, size_t value_bytes, size_t n, unsigned begin_bit,
+                         unsigned end_bit);
+
+const char *rsort_status_string(rsort_status status);
+void rsort_last_error(rsort_error_info *out);
+
+/* Kernel launches issued by the calling host thread since the last reset
+ * (instrumentation for benchmarks; no reference counterpart). */
+uint64_t rsort_launch_count(void);
+void rsort_launch_count_reset(void);
+
+/* Kernel ids reported by rsort_profile_read. */
+enum { RSORT_KERNEL_INIT = 0, RSORT_KERNEL_HISTOGRAM = 1, RSORT_KERNEL_ONESWEEP = 2,
+       RSORT_KERNEL_SINGLE_TILE = 3 };
+
+/* Benchmark instrumentation (no reference counterpart): while enabled, every
+ * kernel launch of the calling host thread is bracketed by CUDA events on its
+ * stream.  rsort_profile_read waits for the recorded launches, writes up to
+ * `capacity` (kernel id, duration in ms) pairs, clears the record and returns
+ * the number of launches recorded. */
+void rsort_profile_enable(int enable);
+size_t rsort_profile_read(int32_t *kernel_ids, float *milliseconds, size_t capacity);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RSORT_B200_H */

@@ -1,0 +1,120 @@
+"""ctypes binding of librsort_b200.so (the C ABI declared in include/rsort_b200.h).
+
+The shared library is the only compute path: if it is missing, loading fails
+loudly instead of falling back to any CPU or library sort.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
+LIB_PATH = os.path.join(LIB_DIR, "librsort_b200.so")
+
+# rsort_key_t
+RSORT_U32, RSORT_I32, RSORT_F32, RSORT_U64, RSORT_I64, RSORT_F64 = range(6)
+
+# rsort_status
+RSORT_OK = 0
+RSORT_INVALID_BIT_RANGE = 1
+RSORT_LENGTH_MISMATCH = 2
+RSORT_WORKSPACE_TOO_SMALL = 3
+RSORT_UNSUPPORTED_TARGET = 4
+RSORT_SIZE_OVERFLOW = 5
+RSORT_CUDA_ERROR = 6
+RSORT_TIMEOUT = 7
+RSORT_BAD_ARGUMENT = 8
+
+# kernel ids of rsort_profile_read
+KERNEL_NAMES = {0: "init", 1: "histogram", 2: "onesweep", 3: "single_tile"}
+
+EXPORTED_SYMBOLS = (
+    "rsort_controls_query",
+    "rsort_keys_buffer",
+    "rsort_pairs_buffer",
+    "rsort_keys",
+    "rsort_pairs",
+    "rsort_check_device_status",
+    "rsort_single_tile_items",
+    "rsort_selector_flips",
+    "rsort_status_string",
+    "rsort_last_error",
+    "rsort_launch_count",
+    "rsort_launch_count_reset",
+    "rsort_profile_enable",
+    "rsort_profile_read",
+)
+
+
+class Controls(ctypes.Structure):
+    _fields_ = [("bins", ctypes.c_size_t), ("lookback", ctypes.c_size_t),
+                ("counters", ctypes.c_size_t)]
+
+
+class ErrorInfo(ctypes.Structure):
+    _fields_ = [("status", ctypes.c_int), ("role", ctypes.c_char_p),
+                ("expected", ctypes.c_size_t), ("actual", ctypes.c_size_t),
+                ("begin_bit", ctypes.c_uint), ("end_bit", ctypes.c_uint),
+                ("key_bits", ctypes.c_uint)]
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def _declare(lib: ctypes.CDLL) -> None:
+    vp, sz, u, i, pi = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint, ctypes.c_int, ctypes.POINTER(ctypes.c_int)
+    lib.rsort_controls_query.argtypes = [i, sz, sz, ctypes.POINTER(Controls)]
+    lib.rsort_controls_query.restype = i
+    lib.rsort_keys_buffer.argtypes = [i, i, vp, vp, sz, u, u, pi, vp, sz, vp, sz, vp, sz, vp]
+    lib.rsort_keys_buffer.restype = i
+    lib.rsort_pairs_buffer.argtypes = [i, i, vp, vp, vp, vp, sz, sz, u, u, pi, vp, sz, vp, sz,
+                                       vp, sz, vp]
+    lib.rsort_pairs_buffer.restype = i
+    lib.rsort_keys.argtypes = [i, i, vp, vp, sz, sz, vp, sz, vp, sz, vp, sz, vp]
+    lib.rsort_keys.restype = i
+    lib.rsort_pairs.argtypes = [i, i, vp, vp, sz, vp, sz, vp, sz, sz, vp, sz, vp, sz, vp, sz, vp]
+    lib.rsort_pairs.restype = i
+    lib.rsort_check_device_status.argtypes = [vp, sz, vp]
+    lib.rsort_check_device_status.restype = i
+    lib.rsort_single_tile_items.argtypes = [i, sz]
+    lib.rsort_single_tile_items.restype = sz
+    lib.rsort_selector_flips.argtypes = [i, sz, sz, u, u]
+    lib.rsort_selector_flips.restype = i
+    lib.rsort_status_string.argtypes = [i]
+    lib.rsort_status_string.restype = ctypes.c_char_p
+    lib.rsort_last_error.argtypes = [ctypes.POINTER(ErrorInfo)]
+    lib.rsort_last_error.restype = None
+    lib.rsort_launch_count.argtypes = []
+    lib.rsort_launch_count.restype = ctypes.c_uint64
+    lib.rsort_launch_count_reset.argtypes = []
+    lib.rsort_launch_count_reset.restype = None
+    lib.rsort_profile_enable.argtypes = [i]
+    lib.rsort_profile_enable.restype = None
+    lib.rsort_profile_read.argtypes = [ctypes.POINTER(ctypes.c_int32),
+                                       ctypes.POINTER(ctypes.c_float), sz]
+    lib.rsort_profile_read.restype = sz
+
+
+def lib() -> ctypes.CDLL:
+    """Load librsort_b200.so once; raise if it has not been built."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise RuntimeError(
+                        f"{LIB_PATH} is missing: build it with "
+                        "`python -c 'import __graft_entry__ as g; g.build()'` "
+                        "(there is no fallback sort)")
+                handle = ctypes.CDLL(LIB_PATH)
+                _declare(handle)
+                _lib = handle
+    return _lib
+
+
+def last_error() -> ErrorInfo:
+    info = ErrorInfo()
+    lib().rsort_last_error(ctypes.byref(info))
+    return info

@@ -1,0 +1,451 @@
+// C ABI of the B200 radix sort: validation, control-region sizing and the
+// pass schedule of one sort.  Replaces the reference's Rust pass control
+// (rccl-cub/src/radix.rs:364-876) together with the kernel-trait seam it
+// drives (rccl-cub/src/radix.rs:205-362).
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "../../include/rsort_b200.h"
+#include "rsort_device.cuh"
+#include "rsort_kernels.cuh"
+
+using namespace rsort;
+
+namespace {
+
+thread_local rsort_error_info g_last_error = {RSORT_OK, "", 0, 0, 0, 0, 0};
+thread_local uint64_t g_launches = 0;
+
+// Benchmark instrumentation: when enabled, every kernel launch of the calling
+// host thread is bracketed by two CUDA events on the launch stream.
+struct ProfiledLaunch {
+    int kernel;
+    cudaEvent_t start, stop;
+};
+thread_local bool g_profile = false;
+thread_local std::vector<ProfiledLaunch> g_profiled;
+thread_local std::vector<cudaEvent_t> g_event_pool;
+
+cudaEvent_t pooled_event() {
+    if (!g_event_pool.empty()) {
+        cudaEvent_t e = g_event_pool.back();
+        g_event_pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+struct LaunchScope {
+    ProfiledLaunch rec{};
+    cudaStream_t stream;
+    bool on;
+    LaunchScope(int kernel, cudaStream_t s) : stream(s), on(g_profile) {
+        ++g_launches;
+        if (on) {
+            rec.kernel = kernel;
+            rec.start = pooled_event();
+            rec.stop = pooled_event();
+            cudaEventRecord(rec.start, stream);
+        }
+    }
+    ~LaunchScope() {
+        if (on) {
+            cudaEventRecord(rec.stop, stream);
+            g_profiled.push_back(rec);
+        }
+    }
+};
+
+rsort_status fail(rsort_status s, const char *role, size_t expected = 0, size_t actual = 0) {
+    g_last_error.status = s;
+    g_last_error.role = role;
+    g_last_error.expected = expected;
+    g_last_error.actual = actual;
+    g_last_error.begin_bit = g_last_error.end_bit = g_last_error.key_bits = 0;
+    return s;
+}
+
+rsort_status fail_bits(unsigned begin, unsigned end, unsigned key_bits) {
+    fail(RSORT_INVALID_BIT_RANGE, "radix bit range");
+    g_last_error.begin_bit = begin;
+    g_last_error.end_bit = end;
+    g_last_error.key_bits = key_bits;
+    return RSORT_INVALID_BIT_RANGE;
+}
+
+rsort_status cuda_fail(cudaError_t e, const char *role) {
+    (void)e;
+    return fail(RSORT_CUDA_ERROR, role);
+}
+
+bool key_ok(rsort_key_t k) { return int(k) >= RSORT_U32 && int(k) <= RSORT_F64; }
+int key_bytes(rsort_key_t k) { return int(k) >= RSORT_U64 ? 8 : 4; }
+int key_kind(rsort_key_t k) {
+    switch (k) {
+        case RSORT_I32:
+        case RSORT_I64: return KIND_SINT;
+        case RSORT_F32:
+        case RSORT_F64: return KIND_FLOAT;
+        default: return KIND_UINT;
+    }
+}
+bool value_ok(size_t vb) { return vb == 0 || vb == 1 || vb == 2 || vb == 4 || vb == 8 || vb == 16; }
+
+struct DeviceInfo {
+    int sm_count = 0;
+    bool supported = false;
+    bool probed = false;
+};
+
+std::mutex g_dev_mutex;
+DeviceInfo g_dev[64];
+
+rsort_status device_info(DeviceInfo *out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return fail(RSORT_UNSUPPORTED_TARGET, "device ordinal");
+    std::lock_guard<std::mutex> lock(g_dev_mutex);
+    DeviceInfo &d = g_dev[dev];
+    if (!d.probed) {
+        int major = 0, sms = 0;
+        e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+        d.sm_count = sms;
+        d.supported = major == 10;  // the kernels are built for sm_100a only
+        d.probed = true;
+    }
+    *out = d;
+    if (!d.supported)
+        return fail(RSORT_UNSUPPORTED_TARGET, "radix sort is built for sm_100a (B200) only");
+    return RSORT_OK;
+}
+
+size_t tiles_for(size_t n, int kb, int vb) {
+    const size_t tile = size_t(onesweep_tile(kb, vb));
+    return (n + tile - 1) / tile;
+}
+
+bool single_route(size_t n, int kb, int vb) { return n <= policy800_single_tile_items(kb, vb); }
+
+struct Controls {
+    uint64_t *bins;
+    size_t nbins;
+    int32_t *lookback;
+    size_t nlookback;
+    int32_t *counters;
+    size_t ncounters;
+};
+
+// rccl-cub/src/radix.rs:388-423 validate_controls, with the lengths taken from
+// rsort_controls_query.
+rsort_status validate_controls(const Controls &c, size_t n, int kb, int vb) {
+    const size_t passes = size_t(kb);  // full-width passes: 8 * kb bits / 8
+    const size_t need_bins = passes * RADIX;
+    const size_t need_lookback = tiles_for(n, kb, vb) * RADIX * 2;
+    if (c.nbins < need_bins) return fail(RSORT_WORKSPACE_TOO_SMALL, "radix bins", need_bins, c.nbins);
+    if (c.nlookback != need_lookback)
+        return fail(RSORT_LENGTH_MISMATCH, "radix lookback", need_lookback, c.nlookback);
+    if (c.ncounters < size_t(CTR_WORDS))
+        return fail(RSORT_WORKSPACE_TOO_SMALL, "radix pass counters", CTR_WORDS, c.ncounters);
+    if (!c.bins || !c.lookback || !c.counters) return fail(RSORT_BAD_ARGUMENT, "null control region");
+    if ((reinterpret_cast<uintptr_t>(c.lookback) & 15) != 0)
+        return fail(RSORT_BAD_ARGUMENT, "radix lookback alignment (16 bytes)");
+    if ((reinterpret_cast<uintptr_t>(c.bins) & 7) != 0)
+        return fail(RSORT_BAD_ARGUMENT, "radix bins alignment (8 bytes)");
+    return RSORT_OK;
+}
+
+// One sort over a DoubleBuffer.  values == nullptr pointers for keys-only.
+rsort_status sort_buffer(rsort_key_t key, int descending, void *kf, void *ks, void *vf, void *vs,
+                         size_t vb, size_t n, unsigned begin_bit, unsigned end_bit,
+                         int *current_is_first, const Controls &c, cudaStream_t stream) {
+    if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
+    if (!value_ok(vb)) return fail(RSORT_BAD_ARGUMENT, "radix value width");
+    if (!current_is_first) return fail(RSORT_BAD_ARGUMENT, "null selector");
+    const int kb = key_bytes(key);
+    const unsigned kbits = unsigned(kb) * 8;
+    // rccl-cub/src/radix.rs:370-376
+    if (begin_bit > end_bit || end_bit > kbits) return fail_bits(begin_bit, end_bit, kbits);
+    const unsigned passes = (end_bit - begin_bit + 7) / 8;
+    // rccl-cub/src/radix.rs:467-469
+    if (n == 0 || passes == 0) return RSORT_OK;
+    if (!kf || !ks || (vb && (!vf || !vs))) return fail(RSORT_BAD_ARGUMENT, "null buffer");
+    const bool cur_first = *current_is_first != 0;
+    void *kin = cur_first ? kf : ks;
+    void *kout = cur_first ? ks : kf;
+    void *vin = cur_first ? vf : vs;
+    void *vout = cur_first ? vs : vf;
+    const int kind = key_kind(key);
+
+    // rccl-cub/src/radix.rs:470-492: single-tile route, one selector flip.
+    DeviceInfo dev;
+    rsort_status st;
+    if (single_route(n, kb, int(vb))) {
+        st = device_info(&dev);
+        if (st != RSORT_OK) return st;
+        SingleArgs a{kin, kout, vin, vout, uint32_t(n), begin_bit, end_bit, kind, descending ? 1 : 0};
+        cudaError_t e;
+        {
+            LaunchScope scope(RSORT_KERNEL_SINGLE_TILE, stream);
+            e = launch_single_tile(kb, int(vb), a, stream);
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "single-tile launch");
+        *current_is_first = cur_first ? 0 : 1;
+        return RSORT_OK;
+    }
+
+    st = validate_controls(c, n, kb, int(vb));
+    if (st != RSORT_OK) return st;
+    st = device_info(&dev);
+    if (st != RSORT_OK) return st;
+    const size_t tiles = tiles_for(n, kb, int(vb));
+    if (tiles > 0x7fffffffull) return fail(RSORT_SIZE_OVERFLOW, "radix tile count");
+
+    cudaError_t e;
+    {
+        LaunchScope scope(RSORT_KERNEL_INIT, stream);
+        // The status word (CTR_STATUS) is sticky: only rsort_check_device_status
+        // clears it, so a give-up in any earlier sort stays visible.
+        e = launch_init(c.bins, size_t(passes) * RADIX, c.counters, CTR_STATUS, stream);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "init launch");
+
+    HistArgs h{};
+    h.keys = kin;
+    h.n = n;
+    h.bins = c.bins;
+    h.lookback = reinterpret_cast<uint64_t *>(c.lookback);
+    h.lookback_words = uint64_t(tiles) * RADIX;
+    h.done = c.counters + CTR_HIST_DONE;
+    h.passes = passes;
+    h.begin_bit = begin_bit;
+    h.end_bit = end_bit;
+    h.kind = kind;
+    h.desc = descending ? 1 : 0;
+    h.vector_ok = (reinterpret_cast<uintptr_t>(kin) & 15) == 0;
+    {
+        LaunchScope scope(RSORT_KERNEL_HISTOGRAM, stream);
+        e = launch_histogram(kb, h, dev.sm_count, stream);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "histogram launch");
+
+    // rccl-cub/src/radix.rs:518-552: one onesweep pass per 8-bit digit, each
+    // flipping the selector.
+    bool first_is_src = cur_first;
+    for (unsigned p = 0; p < passes; ++p) {
+        PassArgs a{};
+        a.keys_in = first_is_src ? kf : ks;
+        a.keys_out = first_is_src ? ks : kf;
+        a.values_in = first_is_src ? vf : vs;
+        a.values_out = first_is_src ? vs : vf;
+        a.n = n;
+        a.bins = c.bins + size_t(p) * RADIX;
+        a.lookback = reinterpret_cast<uint64_t *>(c.lookback);
+        a.tile_counter = c.counters + CTR_TILE + p;
+        a.status = c.counters + CTR_STATUS;
+        a.shift = begin_bit + 8 * p;
+        const unsigned bits = (end_bit - a.shift) < 8 ? (end_bit - a.shift) : 8;
+        a.mask = (1u << bits) - 1;
+        a.kind = kind;
+        a.desc = descending ? 1 : 0;
+        a.first = p == 0;
+        a.last = p + 1 == passes;
+        a.tag = p + 1;
+        {
+            LaunchScope scope(RSORT_KERNEL_ONESWEEP, stream);
+            e = launch_onesweep(kb, int(vb), a, tiles, stream);
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "onesweep launch");
+        first_is_src = !first_is_src;
+    }
+    *current_is_first = first_is_src ? 1 : 0;
+    return RSORT_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+rsort_status rsort_controls_query(rsort_key_t key, size_t value_bytes, size_t n,
+                                  rsort_controls *out) {
+    if (!out) return fail(RSORT_BAD_ARGUMENT, "null output");
+    if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
+    if (!value_ok(value_bytes)) return fail(RSORT_BAD_ARGUMENT, "radix value width");
+    const int kb = key_bytes(key);
+    if (single_route(n, kb, int(value_bytes))) {
+        out->bins = out->lookback = out->counters = 0;
+        return RSORT_OK;
+    }
+    out->bins = size_t(kb) * RADIX;
+    out->lookback = tiles_for(n, kb, int(value_bytes)) * RADIX * 2;
+    out->counters = CTR_WORDS;
+    return RSORT_OK;
+}
+
+rsort_status rsort_keys_buffer(rsort_key_t key, int descending, void *d_first, void *d_second,
+                               size_t n, unsigned begin_bit, unsigned end_bit,
+                               int *current_is_first, uint64_t *bins, size_t nbins,
+                               int32_t *lookback, size_t nlookback, int32_t *counters,
+                               size_t ncounters, rsort_stream_t stream) {
+    Controls c{bins, nbins, lookback, nlookback, counters, ncounters};
+    return sort_buffer(key, descending, d_first, d_second, nullptr, nullptr, 0, n, begin_bit,
+                       end_bit, current_is_first, c, reinterpret_cast<cudaStream_t>(stream));
+}
+
+rsort_status rsort_pairs_buffer(rsort_key_t key, int descending, void *d_keys_first,
+                                void *d_keys_second, void *d_values_first, void *d_values_second,
+                                size_t value_bytes, size_t n, unsigned begin_bit, unsigned end_bit,
+                                int *current_is_first, uint64_t *bins, size_t nbins,
+                                int32_t *lookback, size_t nlookback, int32_t *counters,
+                                size_t ncounters, rsort_stream_t stream) {
+    if (value_bytes == 0) return fail(RSORT_BAD_ARGUMENT, "radix value width");
+    Controls c{bins, nbins, lookback, nlookback, counters, ncounters};
+    return sort_buffer(key, descending, d_keys_first, d_keys_second, d_values_first,
+                       d_values_second, value_bytes, n, begin_bit, end_bit, current_is_first, c,
+                       reinterpret_cast<cudaStream_t>(stream));
+}
+
+rsort_status rsort_keys(rsort_key_t key, int descending, void *d_keys, void *d_scratch,
+                        size_t nscratch, size_t n, uint64_t *bins, size_t nbins, int32_t *lookback,
+                        size_t nlookback, int32_t *counters, size_t ncounters,
+                        rsort_stream_t stream) {
+    if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
+    // rccl-cub/src/radix.rs:591-600
+    if (nscratch != n) return fail(RSORT_LENGTH_MISMATCH, "radix scratch keys", n, nscratch);
+    const int kb = key_bytes(key);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (n > 0 && single_route(n, kb, 0)) {
+        // The single-tile kernel reads its whole input before writing, so it
+        // sorts in place and the reference's copy-back (radix.rs:617-621) is
+        // not needed.
+        int sel = 0;
+        Controls c{bins, nbins, lookback, nlookback, counters, ncounters};
+        return sort_buffer(key, descending, d_keys, d_keys, nullptr, nullptr, 0, n, 0,
+                           unsigned(kb) * 8, &sel, c, s);
+    }
+    int current_is_first = 1;
+    Controls c{bins, nbins, lookback, nlookback, counters, ncounters};
+    rsort_status st = sort_buffer(key, descending, d_keys, d_scratch, nullptr, nullptr, 0, n, 0,
+                                  unsigned(kb) * 8, &current_is_first, c, s);
+    if (st != RSORT_OK) return st;
+    if (!current_is_first && n > 0) {
+        cudaError_t e = cudaMemcpyAsync(d_keys, d_scratch, n * size_t(kb), cudaMemcpyDeviceToDevice, s);
+        if (e != cudaSuccess) return cuda_fail(e, "copy back");
+    }
+    return RSORT_OK;
+}
+
+rsort_status rsort_pairs(rsort_key_t key, int descending, void *d_keys, void *d_values,
+                         size_t value_bytes, void *d_scratch_keys, size_t nscratch_keys,
+                         void *d_scratch_values, size_t nscratch_values, size_t n, uint64_t *bins,
+                         size_t nbins, int32_t *lookback, size_t nlookback, int32_t *counters,
+                         size_t ncounters, rsort_stream_t stream) {
+    if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
+    if (value_bytes == 0 || !value_ok(value_bytes))
+        return fail(RSORT_BAD_ARGUMENT, "radix value width");
+    // rccl-cub/src/radix.rs:833-844
+    if (nscratch_keys != n) return fail(RSORT_LENGTH_MISMATCH, "radix scratch keys", n, nscratch_keys);
+    if (nscratch_values != n)
+        return fail(RSORT_LENGTH_MISMATCH, "radix scratch values", n, nscratch_values);
+    const int kb = key_bytes(key);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    Controls c{bins, nbins, lookback, nlookback, counters, ncounters};
+    if (n > 0 && single_route(n, kb, int(value_bytes))) {
+        int sel = 0;
+        return sort_buffer(key, descending, d_keys, d_keys, d_values, d_values, value_bytes, n, 0,
+                           unsigned(kb) * 8, &sel, c, s);
+    }
+    int current_is_first = 1;
+    rsort_status st = sort_buffer(key, descending, d_keys, d_scratch_keys, d_values,
+                                  d_scratch_values, value_bytes, n, 0, unsigned(kb) * 8,
+                                  &current_is_first, c, s);
+    if (st != RSORT_OK) return st;
+    if (!current_is_first && n > 0) {
+        cudaError_t e = cudaMemcpyAsync(d_keys, d_scratch_keys, n * size_t(kb),
+                                        cudaMemcpyDeviceToDevice, s);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(d_values, d_scratch_values, n * value_bytes,
+                                cudaMemcpyDeviceToDevice, s);
+        if (e != cudaSuccess) return cuda_fail(e, "copy back");
+    }
+    return RSORT_OK;
+}
+
+rsort_status rsort_check_device_status(int32_t *counters, size_t ncounters,
+                                       rsort_stream_t stream) {
+    if (!counters || ncounters < size_t(CTR_WORDS)) return RSORT_OK;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    int32_t word = 0;
+    cudaError_t e = cudaMemcpyAsync(&word, counters + CTR_STATUS, sizeof(word),
+                                    cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "status read");
+    if (word == 0) return RSORT_OK;
+    const int32_t zero = 0;
+    e = cudaMemcpyAsync(counters + CTR_STATUS, &zero, sizeof(zero), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (word == DEV_STATUS_TIMEOUT) return fail(RSORT_TIMEOUT, "radix look-back wait");
+    return fail(RSORT_CUDA_ERROR, "radix scatter bounds check");
+}
+
+size_t rsort_single_tile_items(rsort_key_t key, size_t value_bytes) {
+    if (!key_ok(key)) return 0;
+    return policy800_single_tile_items(key_bytes(key), int(value_bytes));
+}
+
+int rsort_selector_flips(rsort_key_t key, size_t value_bytes, size_t n, unsigned begin_bit,
+                         unsigned end_bit) {
+    if (!key_ok(key) || begin_bit > end_bit || end_bit > unsigned(key_bytes(key)) * 8) return 0;
+    const unsigned passes = (end_bit - begin_bit + 7) / 8;
+    if (n == 0 || passes == 0) return 0;
+    return single_route(n, key_bytes(key), int(value_bytes)) ? 1 : int(passes);
+}
+
+const char *rsort_status_string(rsort_status s) {
+    switch (s) {
+        case RSORT_OK: return "ok";
+        case RSORT_INVALID_BIT_RANGE: return "radix bit range is outside 0..=key_bits or reversed";
+        case RSORT_LENGTH_MISMATCH: return "length does not match required length";
+        case RSORT_WORKSPACE_TOO_SMALL: return "workspace is smaller than required length";
+        case RSORT_UNSUPPORTED_TARGET: return "unsupported target (sm_100a required)";
+        case RSORT_SIZE_OVERFLOW: return "combined device range length overflowed";
+        case RSORT_CUDA_ERROR: return "CUDA error";
+        case RSORT_TIMEOUT: return "bounded device wait gave up";
+        case RSORT_BAD_ARGUMENT: return "invalid argument";
+    }
+    return "unknown status";
+}
+
+void rsort_last_error(rsort_error_info *out) {
+    if (out) *out = g_last_error;
+}
+
+uint64_t rsort_launch_count(void) { return g_launches; }
+void rsort_launch_count_reset(void) { g_launches = 0; }
+
+void rsort_profile_enable(int enable) { g_profile = enable != 0; }
+
+size_t rsort_profile_read(int32_t *kernel_ids, float *milliseconds, size_t capacity) {
+    size_t n = 0;
+    for (const ProfiledLaunch &r : g_profiled) {
+        float ms = 0.f;
+        if (cudaEventSynchronize(r.stop) == cudaSuccess) cudaEventElapsedTime(&ms, r.start, r.stop);
+        if (n < capacity) {
+            if (kernel_ids) kernel_ids[n] = r.kernel;
+            if (milliseconds) milliseconds[n] = ms;
+        }
+        ++n;
+        g_event_pool.push_back(r.start);
+        g_event_pool.push_back(r.stop);
+    }
+    g_profiled.clear();
+    return n;
+}
+
+}  // extern "C"

@@ -1,0 +1,502 @@
+// B200 radix sort kernels: fused multi-digit histogram (+ look-back zeroing and
+// bin scan), the onesweep digit-scatter pass with bounded decoupled look-back,
+// and the one-CTA small-input sort.
+//
+// Reference counterparts (semantics, not structure):
+//   histogram + exclusive sum  rccl-cub/src/ordering_backend/radix.rs:717-895
+//   onesweep keys / pairs      rccl-cub/src/ordering_backend/radix.rs:1022-1687
+//   single tile keys / pairs   rccl-cub/src/ordering_backend/radix.rs:535-715
+#include "rsort_device.cuh"
+#include "rsort_kernels.cuh"
+
+namespace rsort {
+
+template <int VB> struct ValueType;
+template <> struct ValueType<0> { using type = uint8_t; };
+template <> struct ValueType<1> { using type = uint8_t; };
+template <> struct ValueType<2> { using type = uint16_t; };
+template <> struct ValueType<4> { using type = uint32_t; };
+template <> struct ValueType<8> { using type = uint64_t; };
+template <> struct ValueType<16> { using type = uint4; };
+
+// ---------------------------------------------------------------------------
+// Init: zero the bins and the counters region.
+// ---------------------------------------------------------------------------
+__global__ void init_kernel(uint64_t *bins, uint32_t nbins, int *counters, uint32_t ncounters) {
+    for (uint32_t i = threadIdx.x; i < nbins; i += blockDim.x) bins[i] = 0;
+    for (uint32_t i = threadIdx.x; i < ncounters; i += blockDim.x) counters[i] = 0;
+}
+
+// ---------------------------------------------------------------------------
+// Histogram of every digit pass in one read of the keys.  Also zeroes the
+// look-back words for the whole sort, and the last CTA to finish turns the
+// digit counts into global exclusive digit offsets (one scan per pass).
+// ---------------------------------------------------------------------------
+constexpr int HIST_THREADS = 512;
+constexpr int HIST_COPIES = 2;
+
+__device__ __forceinline__ uint64_t block_exclusive_scan_256_u64(uint64_t v, uint64_t *warp_sums) {
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    uint64_t inc = v;
+    if (tid < RADIX) {
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            uint64_t y = __shfl_up_sync(0xffffffffu, inc, off);
+            if (lane >= uint32_t(off)) inc += y;
+        }
+        if (lane == 31) warp_sums[warp] = inc;
+    }
+    __syncthreads();
+    uint64_t prefix = 0;
+#pragma unroll
+    for (int w = 0; w < RADIX / 32; ++w)
+        if (uint32_t(w) < warp) prefix += warp_sums[w];
+    __syncthreads();
+    return prefix + inc - v;
+}
+
+template <typename B>
+__device__ __forceinline__ void hist_count(B raw, const HistArgs &a, uint32_t *h) {
+    const KeyXform xf{a.kind, a.desc};
+    const B o = to_ordered(raw, xf);
+#pragma unroll 1
+    for (uint32_t p = 0; p < a.passes; ++p) {
+        const uint32_t bit = a.begin_bit + 8 * p;
+        const uint32_t bits = min(8u, a.end_bit - bit);
+        const uint32_t d = digit_of(o, a.kind, bit, (1u << bits) - 1);
+        atomicAdd(&h[p * RADIX + d], 1u);
+    }
+}
+
+template <typename B>
+__global__ void __launch_bounds__(HIST_THREADS) histogram_kernel(HistArgs a) {
+    __shared__ uint32_t h[HIST_COPIES][8 * RADIX];
+    __shared__ uint64_t warp_sums[8];
+    __shared__ int is_last;
+    const uint32_t tid = threadIdx.x;
+    for (uint32_t i = tid; i < HIST_COPIES * 8 * RADIX; i += HIST_THREADS) (&h[0][0])[i] = 0;
+
+    // Zero this sort's look-back words (grid-stride, 16-byte stores).
+    {
+        const uint64_t words = a.lookback_words;
+        const uint64_t stride = uint64_t(gridDim.x) * HIST_THREADS;
+        uint4 *lb4 = reinterpret_cast<uint4 *>(a.lookback);
+        const uint64_t n4 = words / 2;
+        for (uint64_t i = uint64_t(blockIdx.x) * HIST_THREADS + tid; i < n4; i += stride)
+            lb4[i] = make_uint4(0, 0, 0, 0);
+        if ((words & 1) && blockIdx.x == 0 && tid == 0) a.lookback[words - 1] = 0;
+    }
+    __syncthreads();
+
+    uint32_t *mine = h[(tid >> 5) % HIST_COPIES];
+    const uint64_t stride = uint64_t(gridDim.x) * HIST_THREADS;
+    const uint64_t gtid = uint64_t(blockIdx.x) * HIST_THREADS + tid;
+    const B *keys = static_cast<const B *>(a.keys);
+    uint64_t scalar_begin = 0;
+    if (a.vector_ok) {
+        constexpr int PER = 16 / sizeof(B);
+        const uint64_t nvec = a.n / PER;
+        const uint4 *kv = reinterpret_cast<const uint4 *>(keys);
+        for (uint64_t i = gtid; i < nvec; i += stride) {
+            const uint4 v = ld_stream(kv + i);
+            if constexpr (sizeof(B) == 4) {
+                hist_count<B>(v.x, a, mine);
+                hist_count<B>(v.y, a, mine);
+                hist_count<B>(v.z, a, mine);
+                hist_count<B>(v.w, a, mine);
+            } else {
+                hist_count<B>((uint64_t(v.y) << 32) | v.x, a, mine);
+                hist_count<B>((uint64_t(v.w) << 32) | v.z, a, mine);
+            }
+        }
+        scalar_begin = nvec * PER;
+    }
+    for (uint64_t i = scalar_begin + gtid; i < a.n; i += stride) hist_count<B>(keys[i], a, mine);
+    __syncthreads();
+
+    for (uint32_t i = tid; i < a.passes * RADIX; i += HIST_THREADS) {
+        uint32_t c = 0;
+#pragma unroll
+        for (int k = 0; k < HIST_COPIES; ++k) c += h[k][i];
+        if (c) atomicAdd(reinterpret_cast<unsigned long long *>(&a.bins[i]),
+                         static_cast<unsigned long long>(c));
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) is_last = atomicAdd(a.done, 1) == int(gridDim.x) - 1;
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    for (uint32_t p = 0; p < a.passes; ++p) {
+        uint64_t v = 0;
+        if (tid < RADIX) v = __ldcg(&a.bins[p * RADIX + tid]);
+        const uint64_t ex = block_exclusive_scan_256_u64(v, warp_sums);
+        if (tid < RADIX) a.bins[p * RADIX + tid] = ex;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Onesweep digit-scatter pass.
+//
+// One CTA per tile; the tile id comes from a per-pass atomic counter, so a
+// tile only ever waits on tiles that were claimed earlier by running CTAs.
+//  1. warp-striped coalesced loads of the tile (pass 0 applies the
+//     raw->ordered transform)
+//  2. stable warp multi-split rank with __match_any_sync over warp-private
+//     256-bin histograms
+//  3. per-digit tile totals, published as look-back aggregates, then a
+//     bounded walk back for the exclusive prefix across tiles
+//  4. keys scattered into shared memory at their tile rank, then written out
+//     by consecutive threads to consecutive addresses of each digit run
+//     (the last pass applies the ordered->raw transform)
+//  5. pairs: values follow through the same shared-memory permutation
+// ---------------------------------------------------------------------------
+template <typename B, int VB, int ITEMS>
+struct OnesweepSmem {
+    static constexpr int THREADS = ONESWEEP_THREADS;
+    static constexpr int WARPS = THREADS / 32;
+    static constexpr int TILE = THREADS * ITEMS;
+    static constexpr int STAGE_ELEM = (VB > int(sizeof(B))) ? VB : int(sizeof(B));
+    static constexpr size_t WHIST = 0;
+    static constexpr size_t TSTART = WHIST + size_t(WARPS) * RADIX * 4;
+    static constexpr size_t GBASE = TSTART + RADIX * 4;
+    static constexpr size_t WSUMS = GBASE + RADIX * 8;
+    static constexpr size_t CTL = WSUMS + 8 * 4;
+    static constexpr size_t STAGE = (CTL + 16 + 15) / 16 * 16;
+    static constexpr size_t DIG = STAGE + size_t(TILE) * STAGE_ELEM;
+    static constexpr size_t BYTES = DIG + (VB > 0 ? size_t(TILE) : 0);
+};
+
+template <typename B, int VB, int ITEMS>
+__global__ void __launch_bounds__(ONESWEEP_THREADS, 2) onesweep_kernel(PassArgs a) {
+    using L = OnesweepSmem<B, VB, ITEMS>;
+    using VT = typename ValueType<VB>::type;
+    constexpr int THREADS = L::THREADS, WARPS = L::WARPS, TILE = L::TILE;
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint32_t *whist = reinterpret_cast<uint32_t *>(smem + L::WHIST);
+    uint32_t *tstart = reinterpret_cast<uint32_t *>(smem + L::TSTART);
+    int64_t *gbase = reinterpret_cast<int64_t *>(smem + L::GBASE);
+    uint32_t *wsums = reinterpret_cast<uint32_t *>(smem + L::WSUMS);
+    int *ctl = reinterpret_cast<int *>(smem + L::CTL);
+    B *skey = reinterpret_cast<B *>(smem + L::STAGE);
+    uint8_t *sdig = smem + L::DIG;
+
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const KeyXform xf{a.kind, a.desc};
+    if (tid == 0) {
+        ctl[0] = atomicAdd(a.tile_counter, 1);
+        ctl[1] = 0;
+    }
+    for (uint32_t i = tid; i < WARPS * RADIX; i += THREADS) whist[i] = 0;
+    __syncthreads();
+
+    const int64_t tile = ctl[0];
+    const uint64_t base = uint64_t(tile) * TILE;
+    const uint64_t remain = a.n - base;
+    const uint32_t count = remain < uint64_t(TILE) ? uint32_t(remain) : uint32_t(TILE);
+    const B *kin = static_cast<const B *>(a.keys_in) + base;
+    const uint32_t seg = warp * 32 * ITEMS;
+
+    B key[ITEMS];
+    uint32_t dig[ITEMS];
+    if (count == uint32_t(TILE)) {
+#pragma unroll
+        for (int j = 0; j < ITEMS; ++j) key[j] = ld_stream(kin + seg + j * 32 + lane);
+    } else {
+#pragma unroll
+        for (int j = 0; j < ITEMS; ++j) {
+            const uint32_t pos = seg + j * 32 + lane;
+            key[j] = pos < count ? kin[pos] : B(0);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {
+        if (a.first) key[j] = to_ordered(key[j], xf);
+        const uint32_t pos = seg + j * 32 + lane;
+        dig[j] = pos < count ? digit_of(key[j], a.kind, a.shift, a.mask) : INVALID_DIGIT;
+    }
+
+    uint32_t rank[ITEMS];
+    uint32_t *wh = whist + warp * RADIX;
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) rank[j] = warp_rank_step(dig[j], wh);
+    __syncthreads();
+
+    uint32_t total = 0;
+    uint64_t *my_lb = a.lookback + uint64_t(tile) * RADIX + tid;
+    if (tid < RADIX) {
+#pragma unroll 4
+        for (int w = 0; w < WARPS; ++w) {
+            const uint32_t t = whist[w * RADIX + tid];
+            whist[w * RADIX + tid] = total;
+            total += t;
+        }
+        st_relaxed_gpu(my_lb, lb_word(tile == 0 ? LB_INCLUSIVE : LB_AGGREGATE, a.tag, total));
+    }
+    const uint32_t tile_excl = block_exclusive_scan_256(total, wsums, nullptr);
+    if (tid < RADIX) {
+        tstart[tid] = tile_excl;
+        uint64_t excl = 0;
+        if (tile > 0) {
+            bool gave_up = false;
+            excl = lookback_exclusive(a.lookback, tile, tid, a.tag, a.status, &gave_up);
+            st_relaxed_gpu(my_lb, lb_word(LB_INCLUSIVE, a.tag, excl + total));
+            if (gave_up) ctl[1] = 1;
+        }
+        gbase[tid] = int64_t(a.bins[tid] + excl) - int64_t(tile_excl);
+    }
+    __syncthreads();
+    const bool abort = ctl[1] != 0;
+
+    bool bad = false;
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {
+        if (dig[j] < RADIX) {
+            const uint32_t r = tstart[dig[j]] + whist[warp * RADIX + dig[j]] + rank[j];
+            rank[j] = r;
+            if (r < count)
+                skey[r] = key[j];
+            else
+                bad = true;
+        }
+    }
+    __syncthreads();
+
+    B *kout = static_cast<B *>(a.keys_out);
+    const int64_t n = int64_t(a.n);
+    for (uint32_t i = tid; i < count; i += THREADS) {
+        const B k = skey[i];
+        const uint32_t d = digit_of(k, a.kind, a.shift, a.mask);
+        if constexpr (VB > 0) sdig[i] = uint8_t(d);
+        const int64_t dst = gbase[d] + int64_t(i);
+        if (!abort) {
+            if (dst >= 0 && dst < n)
+                kout[dst] = a.last ? from_ordered(k, xf) : k;
+            else
+                bad = true;
+        }
+    }
+    if (bad) atomicExch(a.status, DEV_STATUS_BOUNDS);
+
+    if constexpr (VB > 0) {
+        __syncthreads();
+        VT *sval = reinterpret_cast<VT *>(smem + L::STAGE);
+        const VT *vin = static_cast<const VT *>(a.values_in) + base;
+#pragma unroll
+        for (int j = 0; j < ITEMS; ++j) {
+            const uint32_t pos = seg + j * 32 + lane;
+            if (dig[j] < RADIX && rank[j] < count) sval[rank[j]] = vin[pos];
+        }
+        __syncthreads();
+        VT *vout = static_cast<VT *>(a.values_out);
+        for (uint32_t i = tid; i < count; i += THREADS) {
+            const int64_t dst = gbase[sdig[i]] + int64_t(i);
+            if (!abort && dst >= 0 && dst < n) vout[dst] = sval[i];
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Single-tile sort: one CTA sorts n <= the Policy800 single-tile extent in
+// shared memory.  Like the reference's single-tile route it orders by the
+// ascending-space digits of fold(to_ordered_ascending(key)) and reverses each
+// digit for descending order (rccl-cub/src/ordering_kernels.rs:1229-1234,
+// rccl-cub/src/ordering_backend/radix.rs:413-420); the digit width is 8 bits.
+// ---------------------------------------------------------------------------
+template <typename B, int VB>
+struct SingleShape {
+    static constexpr int TILE_MAX = int(policy800_single_tile_items(int(sizeof(B)), VB));
+    static constexpr int ITEMS = (TILE_MAX + SINGLE_THREADS - 1) / SINGLE_THREADS;
+    static constexpr int TILE = ITEMS * SINGLE_THREADS;
+    static constexpr int WARPS = SINGLE_THREADS / 32;
+    static constexpr int VSIZE = VB > 0 ? VB : 1;
+    static constexpr size_t WHIST = 0;
+    static constexpr size_t TSTART = WHIST + size_t(WARPS) * RADIX * 4;
+    static constexpr size_t WSUMS = TSTART + RADIX * 4;
+    static constexpr size_t KEYS = (WSUMS + 8 * 4 + 15) / 16 * 16;
+    static constexpr size_t VALS = KEYS + size_t(TILE) * sizeof(B);
+    static constexpr size_t BYTES = VALS + (VB > 0 ? size_t(TILE) * VSIZE : 0);
+};
+
+template <typename B, int VB>
+__global__ void __launch_bounds__(SINGLE_THREADS, 1) single_tile_kernel(SingleArgs a) {
+    using S = SingleShape<B, VB>;
+    using VT = typename ValueType<VB>::type;
+    constexpr int ITEMS = S::ITEMS, WARPS = S::WARPS, THREADS = SINGLE_THREADS;
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint32_t *whist = reinterpret_cast<uint32_t *>(smem + S::WHIST);
+    uint32_t *tstart = reinterpret_cast<uint32_t *>(smem + S::TSTART);
+    uint32_t *wsums = reinterpret_cast<uint32_t *>(smem + S::WSUMS);
+    B *skey = reinterpret_cast<B *>(smem + S::KEYS);
+    VT *sval = reinterpret_cast<VT *>(smem + S::VALS);
+
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t seg = warp * 32 * ITEMS;
+    const uint32_t n = a.n;
+    const KeyXform asc{a.kind, 0};
+    const B *kin = static_cast<const B *>(a.keys_in);
+    const VT *vin = static_cast<const VT *>(a.values_in);
+
+    B key[ITEMS];
+    VT val[VB > 0 ? ITEMS : 1];
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {
+        const uint32_t pos = seg + j * 32 + lane;
+        key[j] = pos < n ? to_ordered(kin[pos], asc) : B(0);
+        if constexpr (VB > 0) {
+            if (pos < n) val[j] = vin[pos];
+        }
+    }
+
+    for (uint32_t bit = a.begin_bit; bit < a.end_bit; bit += 8) {
+        const uint32_t bits = min(8u, a.end_bit - bit);
+        const uint32_t mask = (1u << bits) - 1;
+        for (uint32_t i = tid; i < WARPS * RADIX; i += THREADS) whist[i] = 0;
+        __syncthreads();
+        uint32_t dig[ITEMS], rank[ITEMS];
+#pragma unroll
+        for (int j = 0; j < ITEMS; ++j) {
+            const uint32_t pos = seg + j * 32 + lane;
+            uint32_t d = digit_of(key[j], a.kind, bit, mask);
+            if (a.desc) d = mask - d;
+            dig[j] = pos < n ? d : INVALID_DIGIT;
+        }
+        uint32_t *wh = whist + warp * RADIX;
+#pragma unroll
+        for (int j = 0; j < ITEMS; ++j) rank[j] = warp_rank_step(dig[j], wh);
+        __syncthreads();
+        uint32_t total = 0;
+        if (tid < RADIX) {
+            for (int w = 0; w < WARPS; ++w) {
+                const uint32_t t = whist[w * RADIX + tid];
+                whist[w * RADIX + tid] = total;
+                total += t;
+            }
+        }
+        const uint32_t ex = block_exclusive_scan_256(total, wsums, nullptr);
+        if (tid < RADIX) tstart[tid] = ex;
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < ITEMS; ++j) {
+            if (dig[j] < RADIX) {
+                const uint32_t r = tstart[dig[j]] + whist[warp * RADIX + dig[j]] + rank[j];
+                if (r < n) {
+                    skey[r] = key[j];
+                    if constexpr (VB > 0) sval[r] = val[j];
+                }
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < ITEMS; ++j) {
+            const uint32_t pos = seg + j * 32 + lane;
+            if (pos < n) {
+                key[j] = skey[pos];
+                if constexpr (VB > 0) val[j] = sval[pos];
+            }
+        }
+        __syncthreads();
+    }
+
+    B *kout = static_cast<B *>(a.keys_out);
+    VT *vout = static_cast<VT *>(a.values_out);
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {
+        const uint32_t pos = seg + j * 32 + lane;
+        if (pos < n) {
+            kout[pos] = from_ordered(key[j], asc);
+            if constexpr (VB > 0) vout[pos] = val[j];
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Launchers
+// ---------------------------------------------------------------------------
+namespace {
+
+template <typename Kernel>
+cudaError_t ensure_smem(Kernel k, size_t bytes) {
+    // cudaFuncSetAttribute is per function and device; calling it each launch
+    // is cheap next to a sort and keeps the launcher stateless.
+    if (bytes <= 48 * 1024) return cudaSuccess;
+    return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+}
+
+template <typename B, int VB>
+cudaError_t onesweep_t(const PassArgs &a, uint64_t tiles, cudaStream_t s) {
+    constexpr int ITEMS = onesweep_items(int(sizeof(B)), VB);
+    using L = OnesweepSmem<B, VB, ITEMS>;
+    auto k = onesweep_kernel<B, VB, ITEMS>;
+    cudaError_t e = ensure_smem(k, L::BYTES);
+    if (e != cudaSuccess) return e;
+    k<<<dim3(uint32_t(tiles)), ONESWEEP_THREADS, L::BYTES, s>>>(a);
+    return cudaGetLastError();
+}
+
+template <typename B, int VB>
+cudaError_t single_t(const SingleArgs &a, cudaStream_t s) {
+    using S = SingleShape<B, VB>;
+    auto k = single_tile_kernel<B, VB>;
+    cudaError_t e = ensure_smem(k, S::BYTES);
+    if (e != cudaSuccess) return e;
+    k<<<1, SINGLE_THREADS, S::BYTES, s>>>(a);
+    return cudaGetLastError();
+}
+
+template <typename B>
+cudaError_t onesweep_vb(int vb, const PassArgs &a, uint64_t tiles, cudaStream_t s) {
+    switch (vb) {
+        case 0: return onesweep_t<B, 0>(a, tiles, s);
+        case 1: return onesweep_t<B, 1>(a, tiles, s);
+        case 2: return onesweep_t<B, 2>(a, tiles, s);
+        case 4: return onesweep_t<B, 4>(a, tiles, s);
+        case 8: return onesweep_t<B, 8>(a, tiles, s);
+        case 16: return onesweep_t<B, 16>(a, tiles, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+template <typename B>
+cudaError_t single_vb(int vb, const SingleArgs &a, cudaStream_t s) {
+    switch (vb) {
+        case 0: return single_t<B, 0>(a, s);
+        case 1: return single_t<B, 1>(a, s);
+        case 2: return single_t<B, 2>(a, s);
+        case 4: return single_t<B, 4>(a, s);
+        case 8: return single_t<B, 8>(a, s);
+        case 16: return single_t<B, 16>(a, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_init(uint64_t *bins, size_t nbins, int *counters, size_t ncounters,
+                        cudaStream_t stream) {
+    init_kernel<<<1, 256, 0, stream>>>(bins, uint32_t(nbins), counters, uint32_t(ncounters));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_histogram(int key_bytes, const HistArgs &a, int sm_count, cudaStream_t stream) {
+    const int blocks = sm_count * 2;
+    if (key_bytes == 4)
+        histogram_kernel<uint32_t><<<blocks, HIST_THREADS, 0, stream>>>(a);
+    else
+        histogram_kernel<uint64_t><<<blocks, HIST_THREADS, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_onesweep(int key_bytes, int value_bytes, const PassArgs &a, uint64_t tiles,
+                            cudaStream_t stream) {
+    return key_bytes == 4 ? onesweep_vb<uint32_t>(value_bytes, a, tiles, stream)
+                          : onesweep_vb<uint64_t>(value_bytes, a, tiles, stream);
+}
+
+cudaError_t launch_single_tile(int key_bytes, int value_bytes, const SingleArgs &a,
+                               cudaStream_t stream) {
+    return key_bytes == 4 ? single_vb<uint32_t>(value_bytes, a, stream)
+                          : single_vb<uint64_t>(value_bytes, a, stream);
+}
+
+}  // namespace rsort

@@ -1,0 +1,96 @@
+// Kernel argument blocks, tile shapes and launch entry points shared by the
+// kernel translation unit and the host pass control.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace rsort {
+
+// Tile shape of the onesweep pass for a (key bytes, value bytes) pair.  The
+// shapes are B200 choices (148 SMs, 228 KB shared memory per SM, two resident
+// 512-thread CTAs per SM), not the reference's Policy800 constants; only the
+// single-tile routing threshold keeps Policy800's value because it decides an
+// observable DoubleBuffer selector outcome.
+constexpr int ONESWEEP_THREADS = 512;
+
+constexpr int onesweep_items(int key_bytes, int value_bytes) {
+    return value_bytes == 0 ? (key_bytes == 4 ? 16 : 8)
+         : value_bytes == 16 ? 6
+         : key_bytes == 4 ? (value_bytes <= 4 ? 12 : 8)
+         : 8;
+}
+
+constexpr int onesweep_tile(int key_bytes, int value_bytes) {
+    return ONESWEEP_THREADS * onesweep_items(key_bytes, value_bytes);
+}
+
+// Policy800 single-tile extent (rccl-cub/src/workspace.rs:23-66):
+// 256 threads * max(1, 19*4 / max(item_size, 4)) items, where item_size is
+// the key size for keys-only and max(key, value) size for pairs.
+constexpr size_t policy800_single_tile_items(int key_bytes, int value_bytes) {
+    const int item = key_bytes > value_bytes ? key_bytes : value_bytes;
+    const int divisor = item > 4 ? item : 4;
+    const int items = 19 * 4 / divisor;
+    return 256u * size_t(items < 1 ? 1 : items);
+}
+
+constexpr int SINGLE_THREADS = 512;
+
+// Counters region layout (int32 words).
+constexpr int CTR_TILE = 0;     // [0, 8): dynamic tile counter of each pass
+constexpr int CTR_HIST_DONE = 8;
+constexpr int CTR_STATUS = 9;
+constexpr int CTR_WORDS = 16;
+
+struct HistArgs {
+    const void *keys;
+    uint64_t n;
+    uint64_t *bins;       // passes * 256
+    uint64_t *lookback;   // zeroed here
+    uint64_t lookback_words;
+    int *done;
+    uint32_t passes;
+    uint32_t begin_bit, end_bit;
+    int kind, desc;
+    int vector_ok;  // keys pointer is 16-byte aligned
+};
+
+struct PassArgs {
+    const void *keys_in;
+    void *keys_out;
+    const void *values_in;
+    void *values_out;
+    uint64_t n;
+    const uint64_t *bins;  // this pass's 256 global digit starts
+    uint64_t *lookback;
+    int *tile_counter;
+    int *status;
+    uint32_t shift, mask;
+    int kind, desc;
+    int first, last;  // apply the raw->ordered / ordered->raw transform
+    uint32_t tag;
+};
+
+struct SingleArgs {
+    const void *keys_in;
+    void *keys_out;
+    const void *values_in;
+    void *values_out;
+    uint32_t n;
+    uint32_t begin_bit, end_bit;
+    int kind, desc;
+};
+
+// Host-side launchers (defined in rsort_kernels.cu).  Each returns the CUDA
+// error of the launch.
+cudaError_t launch_init(uint64_t *bins, size_t nbins, int *counters, size_t ncounters,
+                        cudaStream_t stream);
+cudaError_t launch_histogram(int key_bytes, const HistArgs &a, int sm_count, cudaStream_t stream);
+cudaError_t launch_onesweep(int key_bytes, int value_bytes, const PassArgs &a, uint64_t tiles,
+                            cudaStream_t stream);
+cudaError_t launch_single_tile(int key_bytes, int value_bytes, const SingleArgs &a,
+                               cudaStream_t stream);
+
+}  // namespace rsort

@@ -1,0 +1,356 @@
+"""Host-side mirror of rccl-cub's DeviceRadixSort API over the B200 C ABI.
+
+Same function names, argument meaning and error behaviour as the reference's
+public radix functions (rccl-cub/src/dispatch.rs:2091-2942), workspace types
+(rccl-cub/src/workspace.rs:126-174, 581-706), DoubleBuffer
+(rccl-cub/src/double_buffer.rs:6-130) and Program/Launch binding
+(rccl-cub/src/cuda.rs:741-771).  Device memory is torch CUDA storage; every
+sort runs in librsort_b200.so on the launch's stream and is asynchronous, as
+in the reference.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+from .errors import (BadArgument, DeviceAlgorithmError, LengthMismatch, raise_for)
+
+KEY_TYPES = {
+    torch.uint32: _lib.RSORT_U32,
+    torch.int32: _lib.RSORT_I32,
+    torch.float32: _lib.RSORT_F32,
+    torch.uint64: _lib.RSORT_U64,
+    torch.int64: _lib.RSORT_I64,
+    torch.float64: _lib.RSORT_F64,
+}
+KEY_BITS = {k: (32 if v < _lib.RSORT_U64 else 64) for k, v in KEY_TYPES.items()}
+
+
+class ContextMismatch(DeviceAlgorithmError):
+    """A buffer or stream belongs to another device (rccl-cub/src/cuda.rs:763-765)."""
+
+
+def key_code(dtype: torch.dtype) -> int:
+    try:
+        return KEY_TYPES[dtype]
+    except KeyError:
+        raise BadArgument(f"{dtype} is not a RadixKey (u32/i32/f32/u64/i64/f64)") from None
+
+
+def value_bytes_of(t: torch.Tensor) -> int:
+    """Width of one value item: a 1-D tensor's element size, or the row bytes
+    of a 2-D (n, w) uint8 tensor (w = 1, 2, 4, 8 or 16)."""
+    if t.dim() == 1:
+        return t.element_size()
+    if t.dim() == 2 and t.dtype == torch.uint8:
+        return t.shape[1]
+    raise BadArgument("values must be 1-D, or 2-D uint8 rows")
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+class Launch:
+    """A stream bound to a loaded program (rccl_cub::cuda::Launch)."""
+
+    def __init__(self, device: torch.device, stream: torch.cuda.Stream):
+        self.device = device
+        self.stream = stream
+
+    @property
+    def handle(self) -> int:
+        return self.stream.cuda_stream
+
+    def check(self, *tensors: Optional[torch.Tensor]) -> None:
+        for t in tensors:
+            if t is None:
+                continue
+            if t.device != self.device:
+                raise ContextMismatch(f"tensor on {t.device}, launch on {self.device}")
+            if not t.is_contiguous():
+                raise BadArgument("device ranges must be contiguous")
+
+
+class Program:
+    """The loaded radix-sort library bound to one device (rccl_cub::cuda::Program)."""
+
+    def __init__(self, device: torch.device):
+        self.device = device
+
+    @staticmethod
+    def load(device=None) -> "Program":
+        _lib.lib()
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        device = torch.device(device)
+        if device.type != "cuda":
+            raise ContextMismatch(f"{device} is not a CUDA device")
+        if device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        return Program(device)
+
+    def on(self, stream: Optional[torch.cuda.Stream] = None) -> Launch:
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device)
+        if stream.device != self.device:
+            raise ContextMismatch(f"stream on {stream.device}, program on {self.device}")
+        return Launch(self.device, stream)
+
+
+# ---------------------------------------------------------------------------
+# DoubleBuffer
+# ---------------------------------------------------------------------------
+class DoubleBuffer:
+    """Two same-shaped ranges used by ping-pong sorts.  For pairs each side is
+    a (keys, values) tuple and one selector covers both."""
+
+    def __init__(self, first, second, current_is_first: bool = True):
+        self.first = first
+        self.second = second
+        self._current_is_first = bool(current_is_first)
+
+    @staticmethod
+    def new(first: torch.Tensor, second: torch.Tensor) -> Optional["DoubleBuffer"]:
+        if first.numel() != second.numel():
+            return None
+        return DoubleBuffer(first, second)
+
+    @staticmethod
+    def paired(first: Tuple[torch.Tensor, torch.Tensor],
+               second: Tuple[torch.Tensor, torch.Tensor]) -> Optional["DoubleBuffer"]:
+        n = first[0].shape[0]
+        if first[1].shape[0] != n or second[0].shape[0] != n or second[1].shape[0] != n:
+            return None
+        return DoubleBuffer(tuple(first), tuple(second))
+
+    def __len__(self) -> int:
+        side = self.first[0] if isinstance(self.first, tuple) else self.first
+        return side.shape[0]
+
+    def current_is_first(self) -> bool:
+        return self._current_is_first
+
+    def current(self):
+        return self.first if self._current_is_first else self.second
+
+    def alternate(self):
+        return self.second if self._current_is_first else self.first
+
+    def swap(self) -> None:
+        self._current_is_first = not self._current_is_first
+
+
+# ---------------------------------------------------------------------------
+# Workspaces (caller-owned device memory; the sort itself never allocates)
+# ---------------------------------------------------------------------------
+def controls_counts(key_dtype: torch.dtype, value_bytes: int, n: int) -> Tuple[int, int, int]:
+    out = _lib.Controls()
+    raise_for(_lib.lib().rsort_controls_query(key_code(key_dtype), value_bytes, n,
+                                              ctypes.byref(out)))
+    return out.bins, out.lookback, out.counters
+
+
+@dataclass
+class DeviceRadixSortBufferWorkspace:
+    """bins (u64), lookback (i32), counters (i32): workspace.rs:581-610."""
+    bins: torch.Tensor
+    lookback: torch.Tensor
+    counters: torch.Tensor
+
+    def args(self):
+        return (self.bins.data_ptr(), self.bins.numel(), self.lookback.data_ptr(),
+                self.lookback.numel(), self.counters.data_ptr(), self.counters.numel())
+
+
+@dataclass
+class DeviceRadixSortKeysWorkspace:
+    scratch_keys: torch.Tensor
+    controls: DeviceRadixSortBufferWorkspace
+
+
+@dataclass
+class DeviceRadixSortPairsWorkspace:
+    scratch_keys: torch.Tensor
+    scratch_values: torch.Tensor
+    controls: DeviceRadixSortBufferWorkspace
+
+
+def _controls_for(launch: Launch, key_dtype, value_bytes: int, n: int):
+    nb, nl, nc = controls_counts(key_dtype, value_bytes, n)
+    dev = launch.device
+    return DeviceRadixSortBufferWorkspace(
+        bins=torch.zeros(nb, dtype=torch.int64, device=dev),
+        lookback=torch.zeros(nl, dtype=torch.int32, device=dev),
+        counters=torch.zeros(nc, dtype=torch.int32, device=dev))
+
+
+def device_radix_sort_keys_buffer_workspace(launch: Launch, key_dtype: torch.dtype,
+                                            n: int) -> DeviceRadixSortBufferWorkspace:
+    return _controls_for(launch, key_dtype, 0, n)
+
+
+def device_radix_sort_pairs_buffer_workspace(launch: Launch, key_dtype: torch.dtype,
+                                             value_dtype, n: int) -> DeviceRadixSortBufferWorkspace:
+    return _controls_for(launch, key_dtype, _value_width(value_dtype), n)
+
+
+def device_radix_sort_workspace(launch: Launch, key_dtype: torch.dtype,
+                                n: int) -> DeviceRadixSortKeysWorkspace:
+    """In-place keys workspace (rccl_cub::device_radix_sort_workspace)."""
+    return DeviceRadixSortKeysWorkspace(
+        scratch_keys=torch.zeros(n, dtype=key_dtype, device=launch.device),
+        controls=_controls_for(launch, key_dtype, 0, n))
+
+
+device_radix_sort_keys_workspace = device_radix_sort_workspace
+
+
+def device_radix_sort_pairs_workspace(launch: Launch, key_dtype: torch.dtype, value_dtype,
+                                      n: int) -> DeviceRadixSortPairsWorkspace:
+    vb = _value_width(value_dtype)
+    if isinstance(value_dtype, torch.dtype):
+        sv = torch.zeros(n, dtype=value_dtype, device=launch.device)
+    else:
+        sv = torch.zeros((n, vb), dtype=torch.uint8, device=launch.device)
+    return DeviceRadixSortPairsWorkspace(
+        scratch_keys=torch.zeros(n, dtype=key_dtype, device=launch.device),
+        scratch_values=sv,
+        controls=_controls_for(launch, key_dtype, vb, n))
+
+
+def _value_width(value_dtype) -> int:
+    if isinstance(value_dtype, torch.dtype):
+        return torch.empty(0, dtype=value_dtype).element_size()
+    return int(value_dtype)  # raw byte width for (n, w) uint8 rows
+
+
+# ---------------------------------------------------------------------------
+# Sorts
+# ---------------------------------------------------------------------------
+def _keys_inplace(launch: Launch, keys: torch.Tensor, ws: DeviceRadixSortKeysWorkspace,
+                  descending: bool) -> None:
+    launch.check(keys, ws.scratch_keys)
+    code = key_code(keys.dtype)
+    st = _lib.lib().rsort_keys(code, int(descending), keys.data_ptr(), ws.scratch_keys.data_ptr(),
+                               ws.scratch_keys.numel(), keys.numel(), *ws.controls.args(),
+                               launch.handle)
+    raise_for(st)
+
+
+def device_radix_sort_keys(launch: Launch, keys: torch.Tensor,
+                           workspace: DeviceRadixSortKeysWorkspace) -> None:
+    """Sort keys in ascending radix order (dispatch.rs:2091-2114)."""
+    _keys_inplace(launch, keys, workspace, False)
+
+
+def device_radix_sort_keys_descending(launch: Launch, keys: torch.Tensor,
+                                      workspace: DeviceRadixSortKeysWorkspace) -> None:
+    """Sort keys in descending radix order (dispatch.rs:2117-2140)."""
+    _keys_inplace(launch, keys, workspace, True)
+
+
+def _keys_buffer(launch: Launch, buffers: DoubleBuffer, bit_range: range,
+                 ws: DeviceRadixSortBufferWorkspace, descending: bool) -> None:
+    first, second = buffers.first, buffers.second
+    launch.check(first, second)
+    code = key_code(first.dtype)
+    if second.dtype != first.dtype:
+        raise BadArgument("DoubleBuffer sides differ in key type")
+    sel = ctypes.c_int(1 if buffers.current_is_first() else 0)
+    st = _lib.lib().rsort_keys_buffer(code, int(descending), first.data_ptr(), second.data_ptr(),
+                                      len(buffers), bit_range.start, bit_range.stop,
+                                      ctypes.byref(sel), *ws.args(), launch.handle)
+    raise_for(st)
+    buffers._current_is_first = bool(sel.value)
+
+
+def device_radix_sort_keys_buffer(launch: Launch, buffers: DoubleBuffer, bit_range: range,
+                                  workspace: DeviceRadixSortBufferWorkspace) -> None:
+    """DoubleBuffer keys sort over bits [start, stop) (dispatch.rs:2251-2274)."""
+    _keys_buffer(launch, buffers, bit_range, workspace, False)
+
+
+def device_radix_sort_keys_buffer_descending(launch: Launch, buffers: DoubleBuffer,
+                                             bit_range: range,
+                                             workspace: DeviceRadixSortBufferWorkspace) -> None:
+    _keys_buffer(launch, buffers, bit_range, workspace, True)
+
+
+def _pairs_inplace(launch: Launch, keys: torch.Tensor, values: torch.Tensor,
+                   ws: DeviceRadixSortPairsWorkspace, descending: bool) -> None:
+    launch.check(keys, values, ws.scratch_keys, ws.scratch_values)
+    code = key_code(keys.dtype)
+    # rccl-cub/src/radix.rs:823-831
+    if values.shape[0] != keys.numel():
+        raise LengthMismatch("radix values", keys.numel(), values.shape[0])
+    vb = value_bytes_of(values)
+    if value_bytes_of(ws.scratch_values) != vb:
+        raise BadArgument("scratch values width differs from values")
+    st = _lib.lib().rsort_pairs(code, int(descending), keys.data_ptr(), values.data_ptr(), vb,
+                                ws.scratch_keys.data_ptr(), ws.scratch_keys.numel(),
+                                ws.scratch_values.data_ptr(), ws.scratch_values.shape[0],
+                                keys.numel(), *ws.controls.args(), launch.handle)
+    raise_for(st)
+
+
+def device_radix_sort_pairs(launch: Launch, keys: torch.Tensor, values: torch.Tensor,
+                            workspace: DeviceRadixSortPairsWorkspace) -> None:
+    """Stable key/value sort, ascending (dispatch.rs:2546-2576)."""
+    _pairs_inplace(launch, keys, values, workspace, False)
+
+
+def device_radix_sort_pairs_descending(launch: Launch, keys: torch.Tensor, values: torch.Tensor,
+                                       workspace: DeviceRadixSortPairsWorkspace) -> None:
+    _pairs_inplace(launch, keys, values, workspace, True)
+
+
+def _pairs_buffer(launch: Launch, buffers: DoubleBuffer, bit_range: range,
+                  ws: DeviceRadixSortBufferWorkspace, descending: bool) -> None:
+    (fk, fv), (sk, sv) = buffers.first, buffers.second
+    launch.check(fk, fv, sk, sv)
+    code = key_code(fk.dtype)
+    vb = value_bytes_of(fv)
+    if value_bytes_of(sv) != vb or sk.dtype != fk.dtype:
+        raise BadArgument("DoubleBuffer sides differ in layout")
+    sel = ctypes.c_int(1 if buffers.current_is_first() else 0)
+    st = _lib.lib().rsort_pairs_buffer(code, int(descending), fk.data_ptr(), sk.data_ptr(),
+                                       fv.data_ptr(), sv.data_ptr(), vb, len(buffers),
+                                       bit_range.start, bit_range.stop, ctypes.byref(sel),
+                                       *ws.args(), launch.handle)
+    raise_for(st)
+    buffers._current_is_first = bool(sel.value)
+
+
+def device_radix_sort_pairs_buffer(launch: Launch, buffers: DoubleBuffer, bit_range: range,
+                                   workspace: DeviceRadixSortBufferWorkspace) -> None:
+    """Paired DoubleBuffer sort over bits [start, stop) (dispatch.rs:2846-2894)."""
+    _pairs_buffer(launch, buffers, bit_range, workspace, False)
+
+
+def device_radix_sort_pairs_buffer_descending(launch: Launch, buffers: DoubleBuffer,
+                                              bit_range: range,
+                                              workspace: DeviceRadixSortBufferWorkspace) -> None:
+    _pairs_buffer(launch, buffers, bit_range, workspace, True)
+
+
+def check_device_status(launch: Launch, controls: DeviceRadixSortBufferWorkspace) -> None:
+    """Synchronize the launch's stream and raise DeviceTimeout if a bounded
+    device wait of an earlier sort on these controls gave up."""
+    st = _lib.lib().rsort_check_device_status(
+        controls.counters.data_ptr() if controls.counters.numel() else None,
+        controls.counters.numel(), launch.handle)
+    raise_for(st)
+
+
+def single_tile_items(key_dtype: torch.dtype, value_bytes: int = 0) -> int:
+    return _lib.lib().rsort_single_tile_items(key_code(key_dtype), value_bytes)
+
+
+def selector_flips(key_dtype: torch.dtype, value_bytes: int, n: int, bit_range: range) -> int:
+    return _lib.lib().rsort_selector_flips(key_code(key_dtype), value_bytes, n,
+                                           bit_range.start, bit_range.stop)

@@ -1,0 +1,52 @@
+"""Shared test helpers: golden fixtures and numpy <-> torch transfer."""
+from __future__ import annotations
+
+import json
+import os
+
+import numpy as np
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+NP_OF = {"uint32": np.uint32, "int32": np.int32, "float32": np.float32, "uint64": np.uint64,
+         "int64": np.int64, "float64": np.float64}
+
+
+def load_cases():
+    with open(os.path.join(GOLDEN, "probes.json")) as fh:
+        meta = json.load(fh)
+    arrays = np.load(os.path.join(GOLDEN, "probes.npz"))
+    out = []
+    for m in meta:
+        name = m["name"]
+        case = dict(m)
+        case["keys"] = arrays[f"{name}__keys"]
+        case["expected_keys"] = arrays[f"{name}__expected_keys"]
+        if m["has_values"]:
+            case["values"] = arrays[f"{name}__values"]
+            case["expected_values"] = arrays[f"{name}__expected_values"]
+        if m["has_second"]:
+            case["second"] = arrays[f"{name}__second"]
+        out.append(case)
+    return out
+
+
+def bits(a: np.ndarray) -> np.ndarray:
+    """Raw bit patterns, so float comparisons are bit-exact (NaN payloads, -0.0)."""
+    a = np.ascontiguousarray(a)
+    if a.dtype.itemsize == 4:
+        return a.view(np.uint32)
+    if a.dtype.itemsize == 8:
+        return a.view(np.uint64)
+    if a.dtype.itemsize == 2:
+        return a.view(np.uint16)
+    return a.view(np.uint8)
+
+
+def to_dev(a: np.ndarray, device="cuda"):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+
+
+def to_host(t) -> np.ndarray:
+    return t.cpu().numpy()
