@@ -392,7 +392,7 @@ def run_single(args, workload: Workload):
     kernel_ms = {k: {"launches": len(v), "total_ms": sum(v), "avg_ms": statistics.mean(v)}
                  for k, v in per_kernel.items()}
 
-    e2e = run_e2e(args, workload, keys_h, values_h, dev)
+    e2e = None if args.no_e2e else run_e2e(args, workload, keys_h, values_h, dev)
     del src_k, keys, src_v, values, ws
     torch.cuda.empty_cache()
 
@@ -475,6 +475,8 @@ def main():
     ap.add_argument("--n", type=int, default=None, help="override the workload size")
     ap.add_argument("--impl", default="rccl_b200", choices=["rccl_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true",
+                    help="skip the end-to-end leg (used for profiler runs)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -141,38 +141,64 @@ __device__ __forceinline__ uint64_t lb_word(uint64_t state, uint32_t tag, uint64
 
 // Iteration bound of one look-back wait: with the back-off below this is
 // roughly a second of wall time before the wait gives up.
-constexpr uint32_t LOOKBACK_SPIN_LIMIT = 1u << 23;
+constexpr uint32_t LOOKBACK_SPIN_LIMIT = 1u << 22;
 
-// Walks back from `tile - 1` summing aggregates until an inclusive prefix is
-// found.  Every wait is bounded: on give-up the device status word is set and
-// the (meaningless) partial sum is returned; the caller then skips its global
-// writes.
+// Number of predecessor words one look-back round reads in parallel.  A
+// one-tile-at-a-time walk costs one L2 round trip per predecessor and, at
+// B200 tile rates, has to step back past every tile still in its own
+// look-back; reading a window of predecessors per round keeps the walk to
+// one or two round trips.
+constexpr int LOOKBACK_WINDOW = 16;
+
+// Sums the per-digit counts of all tiles before `tile`: walks back in windows
+// of LOOKBACK_WINDOW predecessors, adding aggregates until it meets an
+// inclusive prefix.  A word that is not yet published is re-polled (bounded):
+// on give-up the device status word is set and the (meaningless) partial sum
+// is returned; the caller then skips its global writes.
 __device__ __forceinline__ uint64_t lookback_exclusive(const uint64_t *lookback, int64_t tile,
                                                        uint32_t digit, uint32_t tag, int *status,
                                                        bool *gave_up) {
     uint64_t exclusive = 0;
     int64_t t = tile - 1;
     uint32_t spins = 0;
+    const uint32_t want_tag = tag & 0x3fff;
     while (t >= 0) {
-        const uint64_t w = ld_relaxed_gpu(lookback + t * RADIX + digit);
-        const uint64_t state = w & (3ull << 62);
-        if (state == 0 || uint32_t((w >> 48) & 0x3fff) != (tag & 0x3fff)) {
-            ++spins;
-            if (spins > 64) __nanosleep(spins > 4096 ? 256 : 32);
-            if ((spins & 1023) == 0 && ld_relaxed_gpu(status) != 0) {
-                *gave_up = true;
-                return exclusive;
+        uint64_t w[LOOKBACK_WINDOW];
+#pragma unroll
+        for (int k = 0; k < LOOKBACK_WINDOW; ++k)
+            w[k] = (t - k >= 0) ? ld_relaxed_gpu(lookback + (t - k) * RADIX + digit)
+                                : lb_word(LB_INCLUSIVE, want_tag, 0);
+        bool stop = false, found = false;
+        int consumed = 0;
+#pragma unroll
+        for (int k = 0; k < LOOKBACK_WINDOW; ++k) {
+            if (!stop) {
+                const uint64_t state = w[k] & (3ull << 62);
+                const bool ready = state != 0 && uint32_t((w[k] >> 48) & 0x3fff) == want_tag;
+                if (!ready) {
+                    stop = true;
+                } else {
+                    exclusive += w[k] & LB_VALUE_MASK;
+                    ++consumed;
+                    if (state == LB_INCLUSIVE) found = stop = true;
+                }
             }
-            if (spins > LOOKBACK_SPIN_LIMIT) {
-                atomicExch(status, DEV_STATUS_TIMEOUT);
-                *gave_up = true;
-                return exclusive;
-            }
-            continue;
         }
-        exclusive += w & LB_VALUE_MASK;
-        if (state == LB_INCLUSIVE) break;
-        --t;
+        if (found) return exclusive;
+        t -= consumed;
+        if (consumed == LOOKBACK_WINDOW) continue;
+        // The word at `t` is not published yet: back off and re-poll.
+        ++spins;
+        if (spins > 8) __nanosleep(spins > 4096 ? 256 : 32);
+        if ((spins & 255) == 0 && ld_relaxed_gpu(status) != 0) {
+            *gave_up = true;
+            return exclusive;
+        }
+        if (spins > LOOKBACK_SPIN_LIMIT) {
+            atomicExch(status, DEV_STATUS_TIMEOUT);
+            *gave_up = true;
+            return exclusive;
+        }
     }
     return exclusive;
 }

@@ -34,6 +34,7 @@ __global__ void init_kernel(uint64_t *bins, uint32_t nbins, int *counters, uint3
 // ---------------------------------------------------------------------------
 constexpr int HIST_THREADS = 512;
 constexpr int HIST_COPIES = 2;
+constexpr int HIST_UNROLL = 4;
 
 __device__ __forceinline__ uint64_t block_exclusive_scan_256_u64(uint64_t v, uint64_t *warp_sums) {
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -94,19 +95,31 @@ __global__ void __launch_bounds__(HIST_THREADS) histogram_kernel(HistArgs a) {
     const B *keys = static_cast<const B *>(a.keys);
     uint64_t scalar_begin = 0;
     if (a.vector_ok) {
+        // HIST_UNROLL independent 16-byte loads per thread are in flight
+        // before any counting, so the SM keeps enough bytes outstanding to
+        // cover DRAM latency.
         constexpr int PER = 16 / sizeof(B);
         const uint64_t nvec = a.n / PER;
         const uint4 *kv = reinterpret_cast<const uint4 *>(keys);
-        for (uint64_t i = gtid; i < nvec; i += stride) {
-            const uint4 v = ld_stream(kv + i);
-            if constexpr (sizeof(B) == 4) {
-                hist_count<B>(v.x, a, mine);
-                hist_count<B>(v.y, a, mine);
-                hist_count<B>(v.z, a, mine);
-                hist_count<B>(v.w, a, mine);
-            } else {
-                hist_count<B>((uint64_t(v.y) << 32) | v.x, a, mine);
-                hist_count<B>((uint64_t(v.w) << 32) | v.z, a, mine);
+        for (uint64_t i = gtid; i < nvec; i += stride * HIST_UNROLL) {
+            uint4 v[HIST_UNROLL];
+#pragma unroll
+            for (int u = 0; u < HIST_UNROLL; ++u) {
+                const uint64_t idx = i + uint64_t(u) * stride;
+                v[u] = idx < nvec ? ld_stream(kv + idx) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int u = 0; u < HIST_UNROLL; ++u) {
+                if (i + uint64_t(u) * stride >= nvec) break;
+                if constexpr (sizeof(B) == 4) {
+                    hist_count<B>(v[u].x, a, mine);
+                    hist_count<B>(v[u].y, a, mine);
+                    hist_count<B>(v[u].z, a, mine);
+                    hist_count<B>(v[u].w, a, mine);
+                } else {
+                    hist_count<B>((uint64_t(v[u].y) << 32) | v[u].x, a, mine);
+                    hist_count<B>((uint64_t(v[u].w) << 32) | v[u].z, a, mine);
+                }
             }
         }
         scalar_begin = nvec * PER;
@@ -156,15 +169,15 @@ struct OnesweepSmem {
     static constexpr int THREADS = ONESWEEP_THREADS;
     static constexpr int WARPS = THREADS / 32;
     static constexpr int TILE = THREADS * ITEMS;
-    static constexpr int STAGE_ELEM = (VB > int(sizeof(B))) ? VB : int(sizeof(B));
+    static constexpr int VSIZE = VB > 0 ? VB : 1;
     static constexpr size_t WHIST = 0;
     static constexpr size_t TSTART = WHIST + size_t(WARPS) * RADIX * 4;
     static constexpr size_t GBASE = TSTART + RADIX * 4;
     static constexpr size_t WSUMS = GBASE + RADIX * 8;
     static constexpr size_t CTL = WSUMS + 8 * 4;
-    static constexpr size_t STAGE = (CTL + 16 + 15) / 16 * 16;
-    static constexpr size_t DIG = STAGE + size_t(TILE) * STAGE_ELEM;
-    static constexpr size_t BYTES = DIG + (VB > 0 ? size_t(TILE) : 0);
+    static constexpr size_t KEYS = (CTL + 16 + 15) / 16 * 16;
+    static constexpr size_t VALS = KEYS + size_t(TILE) * sizeof(B);
+    static constexpr size_t BYTES = VALS + (VB > 0 ? size_t(TILE) * VSIZE : 0);
 };
 
 template <typename B, int VB, int ITEMS>
@@ -178,8 +191,8 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, 2) onesweep_kernel(PassArgs 
     int64_t *gbase = reinterpret_cast<int64_t *>(smem + L::GBASE);
     uint32_t *wsums = reinterpret_cast<uint32_t *>(smem + L::WSUMS);
     int *ctl = reinterpret_cast<int *>(smem + L::CTL);
-    B *skey = reinterpret_cast<B *>(smem + L::STAGE);
-    uint8_t *sdig = smem + L::DIG;
+    B *skey = reinterpret_cast<B *>(smem + L::KEYS);
+    VT *sval = reinterpret_cast<VT *>(smem + L::VALS);
 
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const KeyXform xf{a.kind, a.desc};
@@ -194,12 +207,14 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, 2) onesweep_kernel(PassArgs 
     const uint64_t base = uint64_t(tile) * TILE;
     const uint64_t remain = a.n - base;
     const uint32_t count = remain < uint64_t(TILE) ? uint32_t(remain) : uint32_t(TILE);
+    const bool full = count == uint32_t(TILE);
     const B *kin = static_cast<const B *>(a.keys_in) + base;
     const uint32_t seg = warp * 32 * ITEMS;
 
+    // 1. Warp-striped coalesced loads of keys and values; the values are
+    //    fetched now so their DRAM latency overlaps ranking and look-back.
     B key[ITEMS];
-    uint32_t dig[ITEMS];
-    if (count == uint32_t(TILE)) {
+    if (full) {
 #pragma unroll
         for (int j = 0; j < ITEMS; ++j) key[j] = ld_stream(kin + seg + j * 32 + lane);
     } else {
@@ -209,19 +224,30 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, 2) onesweep_kernel(PassArgs 
             key[j] = pos < count ? kin[pos] : B(0);
         }
     }
+    VT val[VB > 0 ? ITEMS : 1];
+    if constexpr (VB > 0) {
+        const VT *vin = static_cast<const VT *>(a.values_in) + base;
+#pragma unroll
+        for (int j = 0; j < ITEMS; ++j) {
+            const uint32_t pos = seg + j * 32 + lane;
+            if (full || pos < count) val[j] = vin[pos];
+        }
+    }
+
+    // 2. Stable warp multi-split rank over warp-private histograms.
+    uint32_t rank[ITEMS];
+    uint32_t *wh = whist + warp * RADIX;
 #pragma unroll
     for (int j = 0; j < ITEMS; ++j) {
         if (a.first) key[j] = to_ordered(key[j], xf);
         const uint32_t pos = seg + j * 32 + lane;
-        dig[j] = pos < count ? digit_of(key[j], a.kind, a.shift, a.mask) : INVALID_DIGIT;
+        const uint32_t d = (full || pos < count) ? digit_of(key[j], a.kind, a.shift, a.mask)
+                                                 : INVALID_DIGIT;
+        rank[j] = warp_rank_step(d, wh);
     }
-
-    uint32_t rank[ITEMS];
-    uint32_t *wh = whist + warp * RADIX;
-#pragma unroll
-    for (int j = 0; j < ITEMS; ++j) rank[j] = warp_rank_step(dig[j], wh);
     __syncthreads();
 
+    // 3. Per-digit tile totals -> look-back aggregate, warp offsets, tile scan.
     uint32_t total = 0;
     uint64_t *my_lb = a.lookback + uint64_t(tile) * RADIX + tid;
     if (tid < RADIX) {
@@ -234,8 +260,30 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, 2) onesweep_kernel(PassArgs 
         st_relaxed_gpu(my_lb, lb_word(tile == 0 ? LB_INCLUSIVE : LB_AGGREGATE, a.tag, total));
     }
     const uint32_t tile_excl = block_exclusive_scan_256(total, wsums, nullptr);
+    if (tid < RADIX) tstart[tid] = tile_excl;
+    __syncthreads();
+
+    // 4. Scatter keys and values into shared memory at their tile rank (the
+    //    tile rank does not depend on the look-back, so the registers are free
+    //    again before it starts).
+    bool bad = false;
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {
+        const uint32_t pos = seg + j * 32 + lane;
+        if (full || pos < count) {
+            const uint32_t d = digit_of(key[j], a.kind, a.shift, a.mask);
+            const uint32_t r = tstart[d] + whist[warp * RADIX + d] + rank[j];
+            if (r < count) {
+                skey[r] = key[j];
+                if constexpr (VB > 0) sval[r] = val[j];
+            } else {
+                bad = true;
+            }
+        }
+    }
+
+    // 5. Look-back for the exclusive prefix of this tile's digits.
     if (tid < RADIX) {
-        tstart[tid] = tile_excl;
         uint64_t excl = 0;
         if (tile > 0) {
             bool gave_up = false;
@@ -248,52 +296,25 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, 2) onesweep_kernel(PassArgs 
     __syncthreads();
     const bool abort = ctl[1] != 0;
 
-    bool bad = false;
-#pragma unroll
-    for (int j = 0; j < ITEMS; ++j) {
-        if (dig[j] < RADIX) {
-            const uint32_t r = tstart[dig[j]] + whist[warp * RADIX + dig[j]] + rank[j];
-            rank[j] = r;
-            if (r < count)
-                skey[r] = key[j];
-            else
-                bad = true;
-        }
-    }
-    __syncthreads();
-
+    // 6. Consecutive threads write consecutive tile positions, i.e. runs of
+    //    consecutive addresses within each digit's output range.
     B *kout = static_cast<B *>(a.keys_out);
+    VT *vout = static_cast<VT *>(a.values_out);
     const int64_t n = int64_t(a.n);
-    for (uint32_t i = tid; i < count; i += THREADS) {
-        const B k = skey[i];
-        const uint32_t d = digit_of(k, a.kind, a.shift, a.mask);
-        if constexpr (VB > 0) sdig[i] = uint8_t(d);
-        const int64_t dst = gbase[d] + int64_t(i);
-        if (!abort) {
-            if (dst >= 0 && dst < n)
+    if (!abort) {
+        for (uint32_t i = tid; i < count; i += THREADS) {
+            const B k = skey[i];
+            const uint32_t d = digit_of(k, a.kind, a.shift, a.mask);
+            const int64_t dst = gbase[d] + int64_t(i);
+            if (dst >= 0 && dst < n) {
                 kout[dst] = a.last ? from_ordered(k, xf) : k;
-            else
+                if constexpr (VB > 0) vout[dst] = sval[i];
+            } else {
                 bad = true;
+            }
         }
     }
     if (bad) atomicExch(a.status, DEV_STATUS_BOUNDS);
-
-    if constexpr (VB > 0) {
-        __syncthreads();
-        VT *sval = reinterpret_cast<VT *>(smem + L::STAGE);
-        const VT *vin = static_cast<const VT *>(a.values_in) + base;
-#pragma unroll
-        for (int j = 0; j < ITEMS; ++j) {
-            const uint32_t pos = seg + j * 32 + lane;
-            if (dig[j] < RADIX && rank[j] < count) sval[rank[j]] = vin[pos];
-        }
-        __syncthreads();
-        VT *vout = static_cast<VT *>(a.values_out);
-        for (uint32_t i = tid; i < count; i += THREADS) {
-            const int64_t dst = gbase[sdig[i]] + int64_t(i);
-            if (!abort && dst >= 0 && dst < n) vout[dst] = sval[i];
-        }
-    }
 }
 
 // ---------------------------------------------------------------------------

@@ -43,6 +43,13 @@ def run_case(case, launch, execution):
         f = cub.device_radix_sort_pairs_descending if desc else cub.device_radix_sort_pairs
         f(launch, keys, values, ws)
         return keys, values, None
+    if api in ("thrust_sort", "thrust_sort_unstable"):
+        getattr(thrust, api.split("_", 1)[1])(execution, keys)
+        return keys, None, None
+    if api in ("thrust_pairs_sort", "thrust_pairs_sort_unstable"):
+        r = thrust.with_values(keys, values)
+        r.sort(execution) if api.endswith("_sort") else r.sort_unstable(execution)
+        return keys, values, None
     rng = range(*case["bit_range"])
     if api == "keys_buffer":
         second = to_dev(case["second"])
@@ -62,13 +69,6 @@ def run_case(case, launch, execution):
         f(launch, buffers, rng, ws)
         k, v = buffers.current()
         return k, v, buffers
-    if api in ("thrust_sort", "thrust_sort_unstable"):
-        getattr(thrust, api.split("_", 1)[1])(execution, keys)
-        return keys, None, None
-    if api in ("thrust_pairs_sort", "thrust_pairs_sort_unstable"):
-        r = thrust.with_values(keys, values)
-        r.sort(execution) if api.endswith("_sort") else r.sort_unstable(execution)
-        return keys, values, None
     raise AssertionError(api)
 
 
