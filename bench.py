@@ -82,10 +82,9 @@ class Workload:
             keys = np.random.default_rng(1).integers(0, 2**32, self.n, dtype=np.uint64)
             keys = keys[offset:offset + n].astype(np.uint32)
         elif c == 2:
-            rng = np.random.default_rng(2)
-            if offset:
-                rng.integers(0, 2**64, offset, dtype=np.uint64)
-            keys = rng.integers(0, 2**64, n, dtype=np.uint64)
+            bg = np.random.PCG64(2)
+            bg.advance(offset)  # one 64-bit draw per full-range u64 key
+            keys = np.random.Generator(bg).integers(0, 2**64, n, dtype=np.uint64)
         elif c == 3:
             keys = gen_f32_specials(np.random.default_rng(3 + offset), n)
         else:
@@ -466,6 +465,187 @@ def run_e2e(args, workload: Workload, keys_h, values_h, dev):
             "api": "rccl_b200.thrust with_values().sort() (temporary allocation + sync per call)"}
 
 
+# ---------------------------------------------------------------------------
+# N GPUs: distributed sample sort, one process per GPU (weak scaling: every
+# rank holds one workload-sized contiguous shard of the global input)
+# ---------------------------------------------------------------------------
+def run_dist(args, workload: Workload):
+    import ctypes
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    from rccl_b200 import _lib, cub
+    from rccl_b200 import dist as D
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch with torchrun")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                            device_id=dev)
+    m = workload.n
+    keys_h, _ = workload.generate(m, offset=rank * m)
+    src_k = torch.from_numpy(keys_h).to(dev)
+    src_v = None
+    if workload.value is not None:
+        # values = global input index (fits u32 for W * 2^28 < 2^32)
+        src_v = (torch.arange(m, dtype=torch.int64, device=dev) + rank * m).to(torch.int32).view(
+            torch.uint32 if workload.vb == 4 else torch.int32)
+    keys = torch.empty_like(src_k)
+    values = torch.empty_like(src_v) if src_v is not None else None
+    launch = cub.Program.load(dev).on()
+    ops = D.CudaLocalOps(launch)
+    L = _lib.lib()
+
+    def restore():
+        keys.copy_(src_k)
+        if values is not None:
+            values.copy_(src_v)
+
+    for _ in range(args.warmup):
+        restore()
+        out = D.sample_sort(keys, values, workload.desc, ops=ops)
+        del out
+    torch.cuda.synchronize()
+    dist.barrier()
+
+    step_ms, phases = [], {}
+    L.rsort_launch_count_reset()
+    L.rsort_profile_read(None, None, 0)
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            restore()
+            torch.cuda.synchronize()
+            dist.barrier()
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            L.rsort_profile_enable(1)
+            t0.record()
+            out = D.sample_sort(keys, values, workload.desc, ops=ops, timings=phases)
+            t1.record()
+            L.rsort_profile_enable(0)
+            torch.cuda.synchronize()
+            step_ms.append(t0.elapsed_time(t1))
+            if i + 1 < args.steps:
+                del out
+    launches = int(L.rsort_launch_count())
+    cap = 4096
+    kid = (ctypes.c_int32 * cap)()
+    kms = (ctypes.c_float * cap)()
+    nrec = L.rsort_profile_read(kid, kms, cap)
+    per_kernel = {}
+    for i in range(min(nrec, cap)):
+        per_kernel.setdefault(_lib.KERNEL_NAMES.get(kid[i], str(kid[i])), []).append(kms[i])
+
+    # max over ranks of the per-step device time
+    t = torch.tensor(step_ms, dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_max = t.tolist()
+    ph_names = ["local_sort", "partition", "exchange", "merge"]
+    ph = torch.tensor([phases.get(k, 0.0) / args.steps for k in ph_names], dtype=torch.float64,
+                      device=dev)
+    dist.all_reduce(ph, op=dist.ReduceOp.MAX)
+
+    # output checks: local order, rank boundaries, total count, stability
+    ok_k, ok_v = out
+    img = order_image(ok_k.cpu().numpy(), workload.desc)
+    ok = bool(np.all(img[1:] >= img[:-1])) if img.size else True
+    if ok_v is not None and img.size:
+        v = ok_v.cpu().numpy().astype(np.int64)
+        ties = img[1:] == img[:-1]
+        ok = ok and bool(np.all(v[1:][ties] > v[:-1][ties]))
+    edge = torch.tensor([int(img[0]) if img.size else -1, int(img[-1]) if img.size else -1,
+                         img.size], dtype=torch.float64, device=dev)
+    edges = [torch.empty_like(edge) for _ in range(world)]
+    dist.all_gather(edges, edge)
+    oks = torch.tensor([1 if ok else 0], device=dev)
+    dist.all_reduce(oks, op=dist.ReduceOp.MIN)
+    total_out = int(sum(e[2].item() for e in edges))
+    nonempty = [e for e in edges if e[2].item() > 0]
+    bound_ok = all(a[1].item() <= b[0].item() for a, b in zip(nonempty, nonempty[1:]))
+    sent = torch.tensor([float(m * (workload.kb + workload.vb) * (world - 1) / world)],
+                        device=dev)
+    del out, ok_k, ok_v
+
+    # End to end through the public API: pinned host shard -> device, sample
+    # sort, this rank's sorted part -> pinned host.
+    e2e_ms, h2d, d2h = None, 0, 0
+    if not args.no_e2e:
+        hk = torch.from_numpy(keys_h).pin_memory()
+        hv = src_v.cpu().pin_memory() if src_v is not None else None
+        h2d = hk.numel() * hk.element_size() + (hv.numel() * hv.element_size() if hv is not None else 0)
+        e2e_steps = max(1, min(args.steps, 3))
+        times = []
+        for i in range(e2e_steps + 1):
+            torch.cuda.synchronize()
+            dist.barrier()
+            a0 = torch.cuda.Event(enable_timing=True)
+            a1 = torch.cuda.Event(enable_timing=True)
+            a0.record()
+            dk = hk.to(dev, non_blocking=True)
+            dv = hv.to(dev, non_blocking=True) if hv is not None else None
+            rk, rv = D.sample_sort(dk, dv, workload.desc, ops=ops)
+            ok_host = torch.empty(rk.shape, dtype=rk.dtype, pin_memory=True)
+            ok_host.copy_(rk, non_blocking=True)
+            nb = rk.numel() * rk.element_size()
+            if rv is not None:
+                ov_host = torch.empty(rv.shape, dtype=rv.dtype, pin_memory=True)
+                ov_host.copy_(rv, non_blocking=True)
+                nb += rv.numel() * rv.element_size()
+            a1.record()
+            torch.cuda.synchronize()
+            if i > 0:  # first iteration is warm-up
+                times.append(a0.elapsed_time(a1))
+                d2h = max(d2h, nb)
+            del dk, dv, rk, rv
+        tt = torch.tensor(times, dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = sum(tt.tolist()) / len(times)
+    dist.barrier()
+    if rank == 0:
+        total_ms = sum(step_max)
+        value = world * m * args.steps / (total_ms / 1e3)
+        peak, peak_kind = measured_peak()
+        osw = per_kernel.get("onesweep", [])
+        roofline = None
+        if osw:
+            avg_s = statistics.mean(osw) / 1e3
+            achieved = workload.bytes_per_pass / avg_s / 1e9
+            roofline = {"bound": "hbm", "kernel": "onesweep", "achieved": achieved,
+                        "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                        "peak_source": peak_kind, "traffic": profiled_traffic(workload),
+                        "algorithmic_bytes_per_launch": workload.bytes_per_pass,
+                        "avg_launch_ms": avg_s * 1e3}
+        phase_ms = dict(zip(ph_names, ph.tolist()))
+        nvlink_gbs = (sent.item() / (phase_ms["exchange"] / 1e3) / 1e9
+                      if phase_ms["exchange"] > 0 else None)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": np.dtype(workload.key).name, "data": "synthetic (numpy PCG64, seeded)",
+            "config": dict(config_dict(args, workload), n=world * m, per_gpu_n=m,
+                           parallelism=f"sample sort over {world} GPUs (NCCL all-to-all)"),
+            "roofline": roofline, "gpu_launches": launches,
+            "phases_ms_max_over_ranks": phase_ms,
+            "nvlink": {"bytes_per_rank": sent.item(), "achieved_gbs_per_rank": nvlink_gbs,
+                       "peak_gbs": 770.0, "note": "uniform-key estimate of bytes leaving a rank"},
+            "clocks": clocks.summary(),
+            "output_checked": bool(oks.item() == 1 and bound_ok and total_out == world * m),
+            "e2e": None if e2e_ms is None else {
+                "value": world * m / (e2e_ms / 1e3), "unit": UNIT, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "rccl_b200.dist.sample_sort from pinned host shards (max over ranks)"},
+        }
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -485,8 +665,7 @@ def main():
         run_reference(args, workload, rank)
         return
     if world > 1 or args.gpus > 1:
-        from rccl_b200 import dist_bench
-        dist_bench.run(args, workload)
+        run_dist(args, workload)
         return
     run_single(args, workload)
 

@@ -137,6 +137,50 @@ size_t rsort_single_tile_items(rsort_key_t key, size_t value_bytes);
 int rsort_selector_flips(rsort_key_t key, size_t value_bytes, size_t n, unsigned begin_bit,
                          unsigned end_bit);
 
+/* ---------------------------------------------------------------------------
+ * Multi-GPU sample sort device steps.  No reference counterpart: the
+ * reference is single-GPU.  Each rank sorts its contiguous input shard with
+ * rsort_pairs / rsort_keys, then:
+ *   1. rsort_dist_samples   regular samples of the sorted shard
+ *   2. (all-gather of every rank's samples over NCCL, by the caller)
+ *   3. rsort_dist_splitters W-1 splitters from the gathered samples
+ *   4. rsort_dist_bounds    W+1 bucket bounds of the local shard
+ *   5. (all-to-all of the buckets over NCCL, by the caller)
+ *   6. rsort_merge_runs     stable merge of the W received runs
+ * Elements are ordered by the 16-byte composite (order image of the key,
+ * rank << 40 | position in the sorted shard), which is the global stable
+ * order, so the concatenation of the ranks' outputs is the stable sort of the
+ * concatenated inputs.
+ * ------------------------------------------------------------------------- */
+
+/* Composite size in bytes (samples and splitters are arrays of composites). */
+#define RSORT_COMPOSITE_BYTES 16
+/* Largest total sample count rsort_dist_splitters accepts. */
+#define RSORT_MAX_SPLITTER_SAMPLES 8192
+
+rsort_status rsort_dist_samples(rsort_key_t key, int descending, const void *d_sorted_keys,
+                                size_t m, unsigned rank, unsigned samples, void *d_samples,
+                                rsort_stream_t stream);
+rsort_status rsort_dist_splitters(const void *d_samples, size_t total, unsigned world,
+                                  void *d_splitters, rsort_stream_t stream);
+rsort_status rsort_dist_bounds(rsort_key_t key, int descending, const void *d_sorted_keys,
+                               size_t m, unsigned rank, const void *d_splitters, unsigned world,
+                               uint64_t *d_bounds, rsort_stream_t stream);
+
+/* Stable merge of two sorted runs (a then b; equal keys keep a first). */
+rsort_status rsort_merge(rsort_key_t key, int descending, const void *a_keys,
+                         const void *a_values, size_t na, const void *b_keys, const void *b_values,
+                         size_t nb, void *out_keys, void *out_values, size_t value_bytes,
+                         rsort_stream_t stream);
+
+/* Stable merge of `runs` consecutive sorted runs held in keys/values
+ * (run_lengths is a host array).  The result is in keys/values, or in the
+ * scratch buffers when *result_in_scratch is set on return. */
+rsort_status rsort_merge_runs(rsort_key_t key, int descending, void *keys, void *values,
+                              size_t value_bytes, const size_t *run_lengths, unsigned runs,
+                              void *scratch_keys, void *scratch_values, int *result_in_scratch,
+                              rsort_stream_t stream);
+
 const char *rsort_status_string(rsort_status status);
 void rsort_last_error(rsort_error_info *out);
 
@@ -147,7 +191,7 @@ void rsort_launch_count_reset(void);
 
 /* Kernel ids reported by rsort_profile_read. */
 enum { RSORT_KERNEL_INIT = 0, RSORT_KERNEL_HISTOGRAM = 1, RSORT_KERNEL_ONESWEEP = 2,
-       RSORT_KERNEL_SINGLE_TILE = 3 };
+       RSORT_KERNEL_SINGLE_TILE = 3, RSORT_KERNEL_DIST = 4, RSORT_KERNEL_MERGE = 5 };
 
 /* Benchmark instrumentation (no reference counterpart): while enabled, every
  * kernel launch of the calling host thread is bracketed by CUDA events on its

@@ -27,7 +27,8 @@ RSORT_TIMEOUT = 7
 RSORT_BAD_ARGUMENT = 8
 
 # kernel ids of rsort_profile_read
-KERNEL_NAMES = {0: "init", 1: "histogram", 2: "onesweep", 3: "single_tile"}
+KERNEL_NAMES = {0: "init", 1: "histogram", 2: "onesweep", 3: "single_tile", 4: "dist",
+                5: "merge"}
 
 EXPORTED_SYMBOLS = (
     "rsort_controls_query",
@@ -44,6 +45,11 @@ EXPORTED_SYMBOLS = (
     "rsort_launch_count_reset",
     "rsort_profile_enable",
     "rsort_profile_read",
+    "rsort_dist_samples",
+    "rsort_dist_splitters",
+    "rsort_dist_bounds",
+    "rsort_merge",
+    "rsort_merge_runs",
 )
 
 
@@ -95,6 +101,16 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.rsort_profile_read.argtypes = [ctypes.POINTER(ctypes.c_int32),
                                        ctypes.POINTER(ctypes.c_float), sz]
     lib.rsort_profile_read.restype = sz
+    lib.rsort_dist_samples.argtypes = [i, i, vp, sz, u, u, vp, vp]
+    lib.rsort_dist_samples.restype = i
+    lib.rsort_dist_splitters.argtypes = [vp, sz, u, vp, vp]
+    lib.rsort_dist_splitters.restype = i
+    lib.rsort_dist_bounds.argtypes = [i, i, vp, sz, u, vp, u, vp, vp]
+    lib.rsort_dist_bounds.restype = i
+    lib.rsort_merge.argtypes = [i, i, vp, vp, sz, vp, vp, sz, vp, vp, sz, vp]
+    lib.rsort_merge.restype = i
+    lib.rsort_merge_runs.argtypes = [i, i, vp, vp, sz, ctypes.POINTER(sz), u, vp, vp, pi, vp]
+    lib.rsort_merge_runs.restype = i
 
 
 def lib() -> ctypes.CDLL:

@@ -8,6 +8,7 @@
 
 #include "../../include/rsort_b200.h"
 #include "rsort_device.cuh"
+#include "rsort_dist.cuh"
 #include "rsort_kernels.cuh"
 
 using namespace rsort;
@@ -428,6 +429,154 @@ void rsort_last_error(rsort_error_info *out) {
 
 uint64_t rsort_launch_count(void) { return g_launches; }
 void rsort_launch_count_reset(void) { g_launches = 0; }
+
+// ---------------------------------------------------------------------------
+// Multi-GPU sample sort device steps (no reference counterpart).
+// ---------------------------------------------------------------------------
+
+rsort_status rsort_dist_samples(rsort_key_t key, int descending, const void *d_sorted_keys,
+                                size_t m, unsigned rank, unsigned samples, void *d_samples,
+                                rsort_stream_t stream) {
+    if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
+    if (m >= (size_t(1) << POS_BITS) || rank >= (1u << (64 - POS_BITS)))
+        return fail(RSORT_SIZE_OVERFLOW, "sample position");
+    if (samples == 0) return RSORT_OK;
+    if (!d_samples || (m && !d_sorted_keys)) return fail(RSORT_BAD_ARGUMENT, "null buffer");
+    DeviceInfo dev;
+    rsort_status st = device_info(&dev);
+    if (st != RSORT_OK) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    {
+        LaunchScope scope(RSORT_KERNEL_DIST, s);
+        e = launch_samples(key_bytes(key), d_sorted_keys, m, rank, samples,
+                           KeyXform{key_kind(key), descending ? 1 : 0},
+                           static_cast<Composite *>(d_samples), s);
+    }
+    return e == cudaSuccess ? RSORT_OK : cuda_fail(e, "samples launch");
+}
+
+rsort_status rsort_dist_splitters(const void *d_samples, size_t total, unsigned world,
+                                  void *d_splitters, rsort_stream_t stream) {
+    if (world < 1) return fail(RSORT_BAD_ARGUMENT, "world size");
+    if (total > MAX_SPLITTER_SAMPLES)
+        return fail(RSORT_WORKSPACE_TOO_SMALL, "splitter sample set", MAX_SPLITTER_SAMPLES, total);
+    if (world == 1) return RSORT_OK;
+    if (!d_samples || !d_splitters) return fail(RSORT_BAD_ARGUMENT, "null buffer");
+    DeviceInfo dev;
+    rsort_status st = device_info(&dev);
+    if (st != RSORT_OK) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    {
+        LaunchScope scope(RSORT_KERNEL_DIST, s);
+        e = launch_splitters(static_cast<const Composite *>(d_samples), uint32_t(total), world,
+                             static_cast<Composite *>(d_splitters), s);
+    }
+    return e == cudaSuccess ? RSORT_OK : cuda_fail(e, "splitters launch");
+}
+
+rsort_status rsort_dist_bounds(rsort_key_t key, int descending, const void *d_sorted_keys,
+                               size_t m, unsigned rank, const void *d_splitters, unsigned world,
+                               uint64_t *d_bounds, rsort_stream_t stream) {
+    if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
+    if (world < 1 || !d_bounds || (world > 1 && !d_splitters))
+        return fail(RSORT_BAD_ARGUMENT, "null buffer");
+    if (m >= (size_t(1) << POS_BITS)) return fail(RSORT_SIZE_OVERFLOW, "sample position");
+    DeviceInfo dev;
+    rsort_status st = device_info(&dev);
+    if (st != RSORT_OK) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    {
+        LaunchScope scope(RSORT_KERNEL_DIST, s);
+        e = launch_bounds(key_bytes(key), d_sorted_keys, m, rank,
+                          static_cast<const Composite *>(d_splitters), world,
+                          KeyXform{key_kind(key), descending ? 1 : 0}, d_bounds, s);
+    }
+    return e == cudaSuccess ? RSORT_OK : cuda_fail(e, "bounds launch");
+}
+
+rsort_status rsort_merge(rsort_key_t key, int descending, const void *a_keys,
+                         const void *a_values, size_t na, const void *b_keys, const void *b_values,
+                         size_t nb, void *out_keys, void *out_values, size_t value_bytes,
+                         rsort_stream_t stream) {
+    if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
+    if (!value_ok(value_bytes)) return fail(RSORT_BAD_ARGUMENT, "radix value width");
+    if (na + nb == 0) return RSORT_OK;
+    if (!out_keys || (na && !a_keys) || (nb && !b_keys) ||
+        (value_bytes && (!out_values || (na && !a_values) || (nb && !b_values))))
+        return fail(RSORT_BAD_ARGUMENT, "null buffer");
+    if ((na + nb + 2047) / 2048 > 0x7fffffffull) return fail(RSORT_SIZE_OVERFLOW, "merge tiles");
+    DeviceInfo dev;
+    rsort_status st = device_info(&dev);
+    if (st != RSORT_OK) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    MergeArgs p{a_keys, a_values, na, b_keys, b_values, nb, out_keys, out_values,
+                key_kind(key), descending ? 1 : 0};
+    cudaError_t e;
+    {
+        LaunchScope scope(RSORT_KERNEL_MERGE, s);
+        e = launch_merge(key_bytes(key), int(value_bytes), p, s);
+    }
+    return e == cudaSuccess ? RSORT_OK : cuda_fail(e, "merge launch");
+}
+
+rsort_status rsort_merge_runs(rsort_key_t key, int descending, void *keys, void *values,
+                              size_t value_bytes, const size_t *run_lengths, unsigned runs,
+                              void *scratch_keys, void *scratch_values, int *result_in_scratch,
+                              rsort_stream_t stream) {
+    if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
+    if (!value_ok(value_bytes)) return fail(RSORT_BAD_ARGUMENT, "radix value width");
+    if (!result_in_scratch || (runs && !run_lengths)) return fail(RSORT_BAD_ARGUMENT, "null argument");
+    const size_t kb = size_t(key_bytes(key));
+    std::vector<size_t> len(run_lengths, run_lengths + runs), off(runs, 0);
+    size_t total = 0;
+    for (unsigned r = 0; r < runs; ++r) {
+        off[r] = total;
+        total += len[r];
+    }
+    // Pairwise merge tree: runs (0,1), (2,3), ... each round; ties keep the
+    // lower run first, so the result is stable across runs in run order.
+    char *src_k = static_cast<char *>(keys), *dst_k = static_cast<char *>(scratch_keys);
+    char *src_v = static_cast<char *>(values), *dst_v = static_cast<char *>(scratch_values);
+    bool in_scratch = false;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    while (len.size() > 1) {
+        std::vector<size_t> nlen, noff;
+        for (size_t r = 0; r < len.size(); r += 2) {
+            if (r + 1 < len.size()) {
+                rsort_status st = rsort_merge(
+                    key, descending, src_k + off[r] * kb, value_bytes ? src_v + off[r] * value_bytes : nullptr,
+                    len[r], src_k + off[r + 1] * kb,
+                    value_bytes ? src_v + off[r + 1] * value_bytes : nullptr, len[r + 1],
+                    dst_k + off[r] * kb, value_bytes ? dst_v + off[r] * value_bytes : nullptr,
+                    value_bytes, stream);
+                if (st != RSORT_OK) return st;
+                nlen.push_back(len[r] + len[r + 1]);
+            } else {
+                if (len[r]) {
+                    cudaError_t e = cudaMemcpyAsync(dst_k + off[r] * kb, src_k + off[r] * kb,
+                                                    len[r] * kb, cudaMemcpyDeviceToDevice, s);
+                    if (e == cudaSuccess && value_bytes)
+                        e = cudaMemcpyAsync(dst_v + off[r] * value_bytes,
+                                            src_v + off[r] * value_bytes, len[r] * value_bytes,
+                                            cudaMemcpyDeviceToDevice, s);
+                    if (e != cudaSuccess) return cuda_fail(e, "merge run copy");
+                }
+                nlen.push_back(len[r]);
+            }
+            noff.push_back(off[r]);
+        }
+        len.swap(nlen);
+        off.swap(noff);
+        std::swap(src_k, dst_k);
+        std::swap(src_v, dst_v);
+        in_scratch = !in_scratch;
+    }
+    *result_in_scratch = in_scratch ? 1 : 0;
+    return RSORT_OK;
+}
 
 void rsort_profile_enable(int enable) { g_profile = enable != 0; }
 

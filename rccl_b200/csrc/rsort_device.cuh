@@ -65,6 +65,40 @@ __device__ __forceinline__ B from_ordered(B ordered, KeyXform x) {
     return a;
 }
 
+// Compile-time-kind forms used by the onesweep pass: `dmask` is all ones for
+// descending order and zero for ascending, so the direction costs one XOR.
+template <int KIND, typename B>
+__device__ __forceinline__ B to_ordered_k(B raw, B dmask) {
+    using T = KeyBits<B>;
+    if constexpr (KIND == KIND_FLOAT)
+        return raw ^ (B(typename T::Signed(raw) >> (T::WIDTH - 1)) | T::SIGN) ^ dmask;
+    else if constexpr (KIND == KIND_SINT)
+        return raw ^ T::SIGN ^ dmask;
+    else
+        return raw ^ dmask;
+}
+
+template <int KIND, typename B>
+__device__ __forceinline__ B from_ordered_k(B ordered, B dmask) {
+    using T = KeyBits<B>;
+    const B a = ordered ^ dmask;
+    if constexpr (KIND == KIND_FLOAT)
+        return a ^ (T::SIGN | B(~B(typename T::Signed(a) >> (T::WIDTH - 1))));
+    else if constexpr (KIND == KIND_SINT)
+        return a ^ T::SIGN;
+    else
+        return a;
+}
+
+template <int KIND, typename B>
+__device__ __forceinline__ uint32_t digit_k(B ordered, uint32_t shift, uint32_t mask) {
+    using T = KeyBits<B>;
+    if constexpr (KIND == KIND_FLOAT) {
+        if (ordered == B(T::SIGN - 1)) ordered = B(T::SIGN);
+    }
+    return uint32_t(ordered >> shift) & mask;
+}
+
 // The float digit functions fold the ordered image 0x7fff..ff (one of the two
 // zeros) onto 0x8000..00 so that -0.0 and +0.0 are equal radix keys
 // (rccl-cub/src/ordering_backend/radix.rs:257-337).
@@ -187,17 +221,28 @@ __device__ __forceinline__ uint64_t lookback_exclusive(const uint64_t *lookback,
         if (found) return exclusive;
         t -= consumed;
         if (consumed == LOOKBACK_WINDOW) continue;
-        // The word at `t` is not published yet: back off and re-poll.
-        ++spins;
-        if (spins > 8) __nanosleep(spins > 4096 ? 256 : 32);
-        if ((spins & 255) == 0 && ld_relaxed_gpu(status) != 0) {
-            *gave_up = true;
-            return exclusive;
-        }
-        if (spins > LOOKBACK_SPIN_LIMIT) {
-            atomicExch(status, DEV_STATUS_TIMEOUT);
-            *gave_up = true;
-            return exclusive;
+        // The word of tile `t` is not published yet: poll that word alone
+        // (bounded, with back-off) and continue the walk once it is.
+        for (;;) {
+            const uint64_t x = ld_relaxed_gpu(lookback + t * RADIX + digit);
+            const uint64_t state = x & (3ull << 62);
+            if (state != 0 && uint32_t((x >> 48) & 0x3fff) == want_tag) {
+                exclusive += x & LB_VALUE_MASK;
+                if (state == LB_INCLUSIVE) return exclusive;
+                --t;
+                break;
+            }
+            ++spins;
+            if (spins > 8) __nanosleep(spins > 4096 ? 256 : 32);
+            if ((spins & 255) == 0 && ld_relaxed_gpu(status) != 0) {
+                *gave_up = true;
+                return exclusive;
+            }
+            if (spins > LOOKBACK_SPIN_LIMIT) {
+                atomicExch(status, DEV_STATUS_TIMEOUT);
+                *gave_up = true;
+                return exclusive;
+            }
         }
     }
     return exclusive;
@@ -208,20 +253,49 @@ __device__ __forceinline__ uint64_t lookback_exclusive(const uint64_t *lookback,
 // order (item j of lane l sits at segment position j*32 + l), so lane order
 // within one step and step order across steps are both input order.
 // `whist` is this warp's 256-entry running histogram in shared memory.
-// Returns the item's rank among equal digits of this warp processed so far.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t warp_rank_step(uint32_t d, uint32_t *whist) {
+// Pipelined form over a thread's items, RANK_GROUP items at a time: every
+// match of the group is issued first, then the peer-group leaders (highest
+// lane of each group) add the group size to the warp histogram with one
+// shared atomic per group, then every lane fetches its group's base from the
+// leader.  The atomics of one warp reach the shared-memory unit in program
+// order, so item j sees the counts of items 0..j-1 exactly as a serial walk
+// does.  Groups bound the live registers of the pipeline.
+constexpr int RANK_GROUP = 4;
+
+// `digit_at(j)` returns item j's digit (INVALID_DIGIT for padding items).
+template <int ITEMS, typename DigitAt>
+__device__ __forceinline__ void warp_rank_items(DigitAt digit_at, uint32_t (&rank)[ITEMS],
+                                                uint32_t *whist) {
     const uint32_t lane = threadIdx.x & 31;
-    const uint32_t peers = __match_any_sync(0xffffffffu, d);
-    const uint32_t before = __popc(peers & lanemask_lt());
-    const bool last_peer = (peers & lanemask_gt()) == 0;
-    uint32_t base = 0;
-    if (d < RADIX) base = whist[d];
-    __syncwarp();
-    if (last_peer && d < RADIX) whist[d] = base + before + 1;
-    __syncwarp();
-    (void)lane;
-    return base + before;
+    const uint32_t lt = lanemask_lt();
+#pragma unroll
+    for (int g = 0; g < ITEMS; g += RANK_GROUP) {
+        constexpr int G = RANK_GROUP;
+        uint32_t d[G], peers[G], got[G];
+#pragma unroll
+        for (int u = 0; u < G; ++u)
+            if (g + u < ITEMS) {
+                d[u] = digit_at(g + u);
+                peers[u] = __match_any_sync(0xffffffffu, d[u]);
+            }
+#pragma unroll
+        for (int u = 0; u < G; ++u) {
+            if (g + u < ITEMS) {
+                const uint32_t leader = 31 - __clz(peers[u]);
+                got[u] = 0;
+                if (lane == leader && d[u] < RADIX)
+                    got[u] = atomicAdd(&whist[d[u]], __popc(peers[u]));
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < G; ++u) {
+            if (g + u < ITEMS) {
+                const uint32_t leader = 31 - __clz(peers[u]);
+                rank[g + u] = __shfl_sync(0xffffffffu, got[u], leader) + __popc(peers[u] & lt);
+            }
+        }
+    }
 }
 
 // Exclusive scan over 256 values held by threads 0..255 (one per thread).

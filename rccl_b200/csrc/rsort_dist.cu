@@ -1,0 +1,306 @@
+// Device steps of the multi-GPU sample sort (no reference counterpart: the
+// reference is single-GPU).  Every element is ordered by the composite
+// (order image, rank, position in the rank's locally sorted shard), which is
+// the global stable order because the input shards are contiguous slices.
+//
+//   samples    regular samples of the locally sorted shard
+//   splitters  sort the world's samples (bitonic, one CTA) and pick W-1
+//   bounds     lower bound of every splitter in the local shard
+//   merge      stable merge-path merge of two sorted runs (ties: first run)
+#include "rsort_device.cuh"
+#include "rsort_dist.cuh"
+
+namespace rsort {
+
+template <typename B>
+__device__ __forceinline__ uint64_t image_of(B raw, KeyXform xf) {
+    return uint64_t(fold_zero(to_ordered(raw, xf), xf.kind));
+}
+
+// ---------------------------------------------------------------------------
+// Regular samples: sample i sits at floor((i + 1) * m / (S + 1)).
+// ---------------------------------------------------------------------------
+template <typename B>
+__global__ void samples_kernel(const B *keys, uint64_t m, uint32_t rank, uint32_t S,
+                               KeyXform xf, Composite *out) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= S) return;
+    if (m == 0) {
+        out[i] = Composite{~0ull, ~0ull};
+        return;
+    }
+    const uint64_t p = (uint64_t(i) + 1) * m / (uint64_t(S) + 1);
+    out[i] = Composite{image_of(keys[p], xf), (uint64_t(rank) << POS_BITS) | p};
+}
+
+__device__ __forceinline__ bool comp_less(const Composite &a, const Composite &b) {
+    return a.key < b.key || (a.key == b.key && a.pos < b.pos);
+}
+
+// ---------------------------------------------------------------------------
+// Splitters: one CTA bitonic-sorts the padded sample set in shared memory;
+// splitter j (1 <= j < W) is sample floor(j * valid / W).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) splitters_kernel(const Composite *samples, uint32_t total,
+                                                         uint32_t world, Composite *splitters) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    Composite *s = reinterpret_cast<Composite *>(smem_raw);
+    __shared__ uint32_t valid;
+    uint32_t np = 1;
+    while (np < total) np <<= 1;
+    if (threadIdx.x == 0) valid = 0;
+    __syncthreads();
+    uint32_t my_valid = 0;
+    for (uint32_t i = threadIdx.x; i < np; i += blockDim.x) {
+        const Composite c = i < total ? samples[i] : Composite{~0ull, ~0ull};
+        s[i] = c;
+        if (c.pos != ~0ull) ++my_valid;
+    }
+    atomicAdd(&valid, my_valid);
+    __syncthreads();
+    for (uint32_t k = 2; k <= np; k <<= 1) {
+        for (uint32_t j = k >> 1; j > 0; j >>= 1) {
+            for (uint32_t i = threadIdx.x; i < np; i += blockDim.x) {
+                const uint32_t partner = i ^ j;
+                if (partner > i) {
+                    const bool up = (i & k) == 0;
+                    const Composite a = s[i], b = s[partner];
+                    if (comp_less(b, a) == up) {
+                        s[i] = b;
+                        s[partner] = a;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    for (uint32_t j = threadIdx.x + 1; j < world; j += blockDim.x) {
+        splitters[j - 1] = valid ? s[uint64_t(j) * valid / world] : Composite{~0ull, ~0ull};
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Bucket bounds: bounds[j] = #{ local i : (image_i, rank, i) < splitter_j }.
+// ---------------------------------------------------------------------------
+template <typename B>
+__global__ void bounds_kernel(const B *keys, uint64_t m, uint32_t rank, const Composite *splitters,
+                              uint32_t world, KeyXform xf, uint64_t *bounds) {
+    const uint32_t j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j > world) return;
+    if (j == 0) {
+        bounds[0] = 0;
+        return;
+    }
+    if (j == world) {
+        bounds[world] = m;
+        return;
+    }
+    const Composite sp = splitters[j - 1];
+    uint64_t lo = 0, hi = m;
+    while (lo < hi) {
+        const uint64_t mid = lo + (hi - lo) / 2;
+        const Composite c{image_of(keys[mid], xf), (uint64_t(rank) << POS_BITS) | mid};
+        if (comp_less(c, sp))
+            lo = mid + 1;
+        else
+            hi = mid;
+    }
+    bounds[j] = lo;
+}
+
+// ---------------------------------------------------------------------------
+// Stable merge of two sorted runs A then B (ties take A first), merge-path
+// partitioned: every CTA owns MERGE_TILE outputs, finds its A/B split with a
+// binary search on the cross diagonal, stages both segments in shared memory,
+// merges MERGE_ITEMS outputs per thread and writes the tile out coalesced.
+// ---------------------------------------------------------------------------
+constexpr int MERGE_THREADS = 256;
+constexpr int MERGE_ITEMS = 8;
+constexpr int MERGE_TILE = MERGE_THREADS * MERGE_ITEMS;
+
+template <typename B>
+__device__ __forceinline__ uint64_t merge_path(const B *a, uint64_t na, const B *b, uint64_t nb,
+                                               uint64_t diag, KeyXform xf) {
+    uint64_t lo = diag > nb ? diag - nb : 0;
+    uint64_t hi = diag < na ? diag : na;
+    while (lo < hi) {
+        const uint64_t mid = lo + (hi - lo) / 2;
+        if (image_of(a[mid], xf) <= image_of(b[diag - 1 - mid], xf))
+            lo = mid + 1;
+        else
+            hi = mid;
+    }
+    return lo;
+}
+
+template <typename B, int VB>
+struct MergeSmem {
+    static constexpr int VSIZE = VB > 0 ? VB : 1;
+    static constexpr size_t KEYS = 0;                                  // A then B segment
+    static constexpr size_t VALS = KEYS + size_t(MERGE_TILE) * sizeof(B);
+    static constexpr size_t OKEYS = VALS + (VB > 0 ? size_t(MERGE_TILE) * VSIZE : 0);
+    static constexpr size_t OVALS = OKEYS + size_t(MERGE_TILE) * sizeof(B);
+    static constexpr size_t BYTES = OVALS + (VB > 0 ? size_t(MERGE_TILE) * VSIZE : 0);
+};
+
+template <int VB> struct MergeValue;
+template <> struct MergeValue<0> { using type = uint8_t; };
+template <> struct MergeValue<1> { using type = uint8_t; };
+template <> struct MergeValue<2> { using type = uint16_t; };
+template <> struct MergeValue<4> { using type = uint32_t; };
+template <> struct MergeValue<8> { using type = uint64_t; };
+template <> struct MergeValue<16> { using type = uint4; };
+
+template <typename B, int VB>
+__global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(MergeArgs p) {
+    using S = MergeSmem<B, VB>;
+    using VT = typename MergeValue<VB>::type;
+    extern __shared__ __align__(16) uint8_t smem[];
+    B *sk = reinterpret_cast<B *>(smem + S::KEYS);
+    VT *sv = reinterpret_cast<VT *>(smem + S::VALS);
+    B *ok = reinterpret_cast<B *>(smem + S::OKEYS);
+    VT *ov = reinterpret_cast<VT *>(smem + S::OVALS);
+    __shared__ uint64_t split[2];
+    const KeyXform xf{p.kind, p.desc};
+    const B *ak = static_cast<const B *>(p.a_keys);
+    const B *bk = static_cast<const B *>(p.b_keys);
+    const VT *av = static_cast<const VT *>(p.a_values);
+    const VT *bv = static_cast<const VT *>(p.b_values);
+    const uint64_t total = p.na + p.nb;
+    const uint64_t d0 = uint64_t(blockIdx.x) * MERGE_TILE;
+    const uint64_t d1 = d0 + MERGE_TILE < total ? d0 + MERGE_TILE : total;
+    if (threadIdx.x < 2)
+        split[threadIdx.x] = merge_path(ak, p.na, bk, p.nb, threadIdx.x == 0 ? d0 : d1, xf);
+    __syncthreads();
+    const uint64_t a0 = split[0], a1 = split[1];
+    const uint64_t b0 = d0 - a0, b1 = d1 - a1;
+    const uint32_t la = uint32_t(a1 - a0), lb = uint32_t(b1 - b0);
+    for (uint32_t i = threadIdx.x; i < la + lb; i += MERGE_THREADS) {
+        if (i < la) {
+            sk[i] = ak[a0 + i];
+            if constexpr (VB > 0) sv[i] = av[a0 + i];
+        } else {
+            sk[i] = bk[b0 + i - la];
+            if constexpr (VB > 0) sv[i] = bv[b0 + i - la];
+        }
+    }
+    __syncthreads();
+    // Per-thread merge path inside the staged tile.
+    const B *ta = sk;
+    const B *tb = sk + la;
+    const uint32_t n = la + lb;
+    const uint32_t diag = min(uint32_t(threadIdx.x) * MERGE_ITEMS, n);
+    uint32_t lo = diag > lb ? diag - lb : 0, hi = diag < la ? diag : la;
+    while (lo < hi) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (image_of(ta[mid], xf) <= image_of(tb[diag - 1 - mid], xf))
+            lo = mid + 1;
+        else
+            hi = mid;
+    }
+    uint32_t ia = lo, ib = diag - lo;
+#pragma unroll
+    for (int k = 0; k < MERGE_ITEMS; ++k) {
+        const uint32_t o = diag + k;
+        if (o < n) {
+            bool take_a;
+            if (ia >= la) take_a = false;
+            else if (ib >= lb) take_a = true;
+            else take_a = image_of(ta[ia], xf) <= image_of(tb[ib], xf);
+            const uint32_t src = take_a ? ia : la + ib;
+            ok[o] = sk[src];
+            if constexpr (VB > 0) ov[o] = sv[src];
+            if (take_a) ++ia; else ++ib;
+        }
+    }
+    __syncthreads();
+    B *outk = static_cast<B *>(p.out_keys) + d0;
+    VT *outv = static_cast<VT *>(p.out_values) + d0;
+    for (uint32_t i = threadIdx.x; i < n; i += MERGE_THREADS) {
+        outk[i] = ok[i];
+        if constexpr (VB > 0) outv[i] = ov[i];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Launchers
+// ---------------------------------------------------------------------------
+namespace {
+
+template <typename B, int VB>
+cudaError_t merge_t(const MergeArgs &p, cudaStream_t s) {
+    using S = MergeSmem<B, VB>;
+    const uint64_t total = p.na + p.nb;
+    if (total == 0) return cudaSuccess;
+    const uint64_t blocks = (total + MERGE_TILE - 1) / MERGE_TILE;
+    auto k = merge_kernel<B, VB>;
+    if (S::BYTES > 48 * 1024) {
+        cudaError_t e =
+            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(S::BYTES));
+        if (e != cudaSuccess) return e;
+    }
+    k<<<dim3(uint32_t(blocks)), MERGE_THREADS, S::BYTES, s>>>(p);
+    return cudaGetLastError();
+}
+
+template <typename B>
+cudaError_t merge_vb(int vb, const MergeArgs &p, cudaStream_t s) {
+    switch (vb) {
+        case 0: return merge_t<B, 0>(p, s);
+        case 1: return merge_t<B, 1>(p, s);
+        case 2: return merge_t<B, 2>(p, s);
+        case 4: return merge_t<B, 4>(p, s);
+        case 8: return merge_t<B, 8>(p, s);
+        case 16: return merge_t<B, 16>(p, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_samples(int key_bytes, const void *keys, uint64_t m, uint32_t rank, uint32_t S,
+                           KeyXform xf, Composite *out, cudaStream_t s) {
+    const uint32_t blocks = (S + 255) / 256;
+    if (blocks == 0) return cudaSuccess;
+    if (key_bytes == 4)
+        samples_kernel<uint32_t><<<blocks, 256, 0, s>>>(static_cast<const uint32_t *>(keys), m,
+                                                       rank, S, xf, out);
+    else
+        samples_kernel<uint64_t><<<blocks, 256, 0, s>>>(static_cast<const uint64_t *>(keys), m,
+                                                       rank, S, xf, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_splitters(const Composite *samples, uint32_t total, uint32_t world,
+                             Composite *splitters, cudaStream_t s) {
+    uint32_t np = 1;
+    while (np < total) np <<= 1;
+    const size_t bytes = size_t(np) * sizeof(Composite);
+    if (bytes > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(splitters_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+        if (e != cudaSuccess) return e;
+    }
+    splitters_kernel<<<1, 1024, bytes, s>>>(samples, total, world, splitters);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_bounds(int key_bytes, const void *keys, uint64_t m, uint32_t rank,
+                          const Composite *splitters, uint32_t world, KeyXform xf,
+                          uint64_t *bounds, cudaStream_t s) {
+    const uint32_t blocks = (world + 1 + 63) / 64;
+    if (key_bytes == 4)
+        bounds_kernel<uint32_t><<<blocks, 64, 0, s>>>(static_cast<const uint32_t *>(keys), m, rank,
+                                                     splitters, world, xf, bounds);
+    else
+        bounds_kernel<uint64_t><<<blocks, 64, 0, s>>>(static_cast<const uint64_t *>(keys), m, rank,
+                                                     splitters, world, xf, bounds);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_merge(int key_bytes, int value_bytes, const MergeArgs &p, cudaStream_t s) {
+    return key_bytes == 4 ? merge_vb<uint32_t>(value_bytes, p, s)
+                          : merge_vb<uint64_t>(value_bytes, p, s);
+}
+
+}  // namespace rsort

@@ -1,0 +1,44 @@
+// Shared declarations of the sample-sort device steps.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "rsort_device.cuh"
+
+namespace rsort {
+
+// Composite sort position of one element: order image of the key, then
+// (rank << POS_BITS | position in the rank's locally sorted shard).
+struct Composite {
+    uint64_t key;
+    uint64_t pos;
+};
+constexpr int POS_BITS = 40;
+
+// Largest sample set the one-CTA splitter kernel sorts (power of two; 16 bytes
+// per composite in shared memory).
+constexpr uint32_t MAX_SPLITTER_SAMPLES = 8192;
+
+struct MergeArgs {
+    const void *a_keys;
+    const void *a_values;
+    uint64_t na;
+    const void *b_keys;
+    const void *b_values;
+    uint64_t nb;
+    void *out_keys;
+    void *out_values;
+    int kind, desc;
+};
+
+cudaError_t launch_samples(int key_bytes, const void *keys, uint64_t m, uint32_t rank, uint32_t S,
+                           KeyXform xf, Composite *out, cudaStream_t s);
+cudaError_t launch_splitters(const Composite *samples, uint32_t total, uint32_t world,
+                             Composite *splitters, cudaStream_t s);
+cudaError_t launch_bounds(int key_bytes, const void *keys, uint64_t m, uint32_t rank,
+                          const Composite *splitters, uint32_t world, KeyXform xf,
+                          uint64_t *bounds, cudaStream_t s);
+cudaError_t launch_merge(int key_bytes, int value_bytes, const MergeArgs &p, cudaStream_t s);
+
+}  // namespace rsort

@@ -180,7 +180,7 @@ struct OnesweepSmem {
     static constexpr size_t BYTES = VALS + (VB > 0 ? size_t(TILE) * VSIZE : 0);
 };
 
-template <typename B, int VB, int ITEMS>
+template <typename B, int VB, int ITEMS, int KIND>
 __global__ void __launch_bounds__(ONESWEEP_THREADS, 2) onesweep_kernel(PassArgs a) {
     using L = OnesweepSmem<B, VB, ITEMS>;
     using VT = typename ValueType<VB>::type;
@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, 2) onesweep_kernel(PassArgs 
     VT *sval = reinterpret_cast<VT *>(smem + L::VALS);
 
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const KeyXform xf{a.kind, a.desc};
+    const B dmask = a.desc ? B(~B(0)) : B(0);
     if (tid == 0) {
         ctl[0] = atomicAdd(a.tile_counter, 1);
         ctl[1] = 0;
@@ -236,15 +236,16 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, 2) onesweep_kernel(PassArgs 
 
     // 2. Stable warp multi-split rank over warp-private histograms.
     uint32_t rank[ITEMS];
-    uint32_t *wh = whist + warp * RADIX;
+    if (a.first) {
 #pragma unroll
-    for (int j = 0; j < ITEMS; ++j) {
-        if (a.first) key[j] = to_ordered(key[j], xf);
-        const uint32_t pos = seg + j * 32 + lane;
-        const uint32_t d = (full || pos < count) ? digit_of(key[j], a.kind, a.shift, a.mask)
-                                                 : INVALID_DIGIT;
-        rank[j] = warp_rank_step(d, wh);
+        for (int j = 0; j < ITEMS; ++j) key[j] = to_ordered_k<KIND>(key[j], dmask);
     }
+    warp_rank_items<ITEMS>(
+        [&](int j) {
+            return (full || seg + j * 32 + lane < count) ? digit_k<KIND>(key[j], a.shift, a.mask)
+                                                         : INVALID_DIGIT;
+        },
+        rank, whist + warp * RADIX);
     __syncthreads();
 
     // 3. Per-digit tile totals -> look-back aggregate, warp offsets, tile scan.
@@ -271,7 +272,7 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, 2) onesweep_kernel(PassArgs 
     for (int j = 0; j < ITEMS; ++j) {
         const uint32_t pos = seg + j * 32 + lane;
         if (full || pos < count) {
-            const uint32_t d = digit_of(key[j], a.kind, a.shift, a.mask);
+            const uint32_t d = digit_k<KIND>(key[j], a.shift, a.mask);
             const uint32_t r = tstart[d] + whist[warp * RADIX + d] + rank[j];
             if (r < count) {
                 skey[r] = key[j];
@@ -304,10 +305,10 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, 2) onesweep_kernel(PassArgs 
     if (!abort) {
         for (uint32_t i = tid; i < count; i += THREADS) {
             const B k = skey[i];
-            const uint32_t d = digit_of(k, a.kind, a.shift, a.mask);
+            const uint32_t d = digit_k<KIND>(k, a.shift, a.mask);
             const int64_t dst = gbase[d] + int64_t(i);
             if (dst >= 0 && dst < n) {
-                kout[dst] = a.last ? from_ordered(k, xf) : k;
+                kout[dst] = a.last ? from_ordered_k<KIND>(k, dmask) : k;
                 if constexpr (VB > 0) vout[dst] = sval[i];
             } else {
                 bad = true;
@@ -382,9 +383,7 @@ __global__ void __launch_bounds__(SINGLE_THREADS, 1) single_tile_kernel(SingleAr
             if (a.desc) d = mask - d;
             dig[j] = pos < n ? d : INVALID_DIGIT;
         }
-        uint32_t *wh = whist + warp * RADIX;
-#pragma unroll
-        for (int j = 0; j < ITEMS; ++j) rank[j] = warp_rank_step(dig[j], wh);
+        warp_rank_items<ITEMS>([&](int j) { return dig[j]; }, rank, whist + warp * RADIX);
         __syncthreads();
         uint32_t total = 0;
         if (tid < RADIX) {
@@ -448,7 +447,9 @@ template <typename B, int VB>
 cudaError_t onesweep_t(const PassArgs &a, uint64_t tiles, cudaStream_t s) {
     constexpr int ITEMS = onesweep_items(int(sizeof(B)), VB);
     using L = OnesweepSmem<B, VB, ITEMS>;
-    auto k = onesweep_kernel<B, VB, ITEMS>;
+    auto k = a.kind == KIND_FLOAT  ? onesweep_kernel<B, VB, ITEMS, KIND_FLOAT>
+             : a.kind == KIND_SINT ? onesweep_kernel<B, VB, ITEMS, KIND_SINT>
+                                   : onesweep_kernel<B, VB, ITEMS, KIND_UINT>;
     cudaError_t e = ensure_smem(k, L::BYTES);
     if (e != cudaSuccess) return e;
     k<<<dim3(uint32_t(tiles)), ONESWEEP_THREADS, L::BYTES, s>>>(a);

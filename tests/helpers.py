@@ -50,3 +50,23 @@ def to_dev(a: np.ndarray, device="cuda"):
 
 def to_host(t) -> np.ndarray:
     return t.cpu().numpy()
+
+
+def order_image(keys: np.ndarray, descending: bool = False) -> np.ndarray:
+    """Unsigned image whose ascending order is the reference's sort order for
+    full-width sorts (to_ordered + float zero fold, vectorized)."""
+    w = keys.dtype.itemsize * 8
+    ut = np.uint32 if w == 32 else np.uint64
+    u = np.ascontiguousarray(keys).view(ut)
+    sign = ut(1 << (w - 1))
+    if keys.dtype.kind == "f":
+        o = np.where((u & sign) != 0, ~u, u ^ sign)
+    elif keys.dtype.kind == "i":
+        o = u ^ sign
+    else:
+        o = u.copy()
+    if descending:
+        o = ~o
+    if keys.dtype.kind == "f":
+        o = np.where(o == sign - ut(1), sign, o)
+    return o.astype(np.uint64)
