@@ -173,16 +173,16 @@ __device__ __forceinline__ uint64_t lb_word(uint64_t state, uint32_t tag, uint64
     return state | (uint64_t(tag & 0x3fff) << 48) | (value & LB_VALUE_MASK);
 }
 
-// Iteration bound of one look-back wait: with the back-off below this is
-// roughly a second of wall time before the wait gives up.
-constexpr uint32_t LOOKBACK_SPIN_LIMIT = 1u << 22;
-
 // Number of predecessor words one look-back round reads in parallel.  A
 // one-tile-at-a-time walk costs one L2 round trip per predecessor and, at
 // B200 tile rates, has to step back past every tile still in its own
 // look-back; reading a window of predecessors per round keeps the walk to
 // one or two round trips.
 constexpr int LOOKBACK_WINDOW = 16;
+
+// Iteration bound of one look-back wait: with the back-off below this is
+// roughly a second of wall time before the wait gives up.
+constexpr uint32_t LOOKBACK_SPIN_LIMIT = 1u << 22;
 
 // Sums the per-digit counts of all tiles before `tile`: walks back in windows
 // of LOOKBACK_WINDOW predecessors, adding aggregates until it meets an
@@ -263,10 +263,61 @@ __device__ __forceinline__ uint64_t lookback_exclusive(const uint64_t *lookback,
 // does.  Groups bound the live registers of the pipeline.
 constexpr int RANK_GROUP = 4;
 
+// Lanes of the warp holding the same 8-bit digit: one ballot per digit bit
+// (eight votes and eight logic ops).  On sm_100 this is far cheaper than
+// __match_any_sync for 8-bit labels (measured: a 16-item rank step took ~9 us
+// per 8192-key tile with match.any).  Padding items carry INVALID_DIGIT; a
+// ninth vote on validity keeps them out of real digits' groups.
+__device__ __forceinline__ uint32_t match_digit(uint32_t d, bool check_valid) {
+    uint32_t peers = 0xffffffffu;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+        const bool set = (d >> b) & 1u;
+        const uint32_t v = __ballot_sync(0xffffffffu, set);
+        peers &= set ? v : ~v;
+    }
+    if (check_valid) {
+        const bool valid = d < RADIX;
+        const uint32_t v = __ballot_sync(0xffffffffu, valid);
+        peers &= valid ? v : ~v;
+    }
+    return peers;
+}
+
+// Peer masks through shared memory: every lane ORs its lane bit into the
+// warp's mask word of its digit, reads the word back after a warp barrier, and
+// the group leader clears it after a second barrier.  About a dozen
+// instructions per item (against ~30 for the ballot network) with no
+// ordering assumption beyond __syncwarp.  `wmask` is the warp's 256-word mask
+// array, all zero between uses.
+template <int ITEMS, typename DigitAt>
+__device__ __forceinline__ void warp_rank_items_or(DigitAt digit_at, uint32_t (&rank)[ITEMS],
+                                                   uint32_t *whist, uint32_t *wmask) {
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t lt = lanemask_lt(), bit = 1u << lane;
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {
+        const uint32_t d = digit_at(j);
+        const bool valid = d < RADIX;
+        if (valid) atomicOr(&wmask[d], bit);
+        __syncwarp();
+        const uint32_t peers = valid ? wmask[d] : 0u;
+        __syncwarp();
+        const uint32_t leader = 31 - __clz(peers);
+        uint32_t got = 0;
+        if (valid && lane == leader) {
+            got = atomicAdd(&whist[d], __popc(peers));
+            wmask[d] = 0;
+        }
+        rank[j] = __shfl_sync(0xffffffffu, got, leader & 31) + __popc(peers & lt);
+    }
+    __syncwarp();
+}
+
 // `digit_at(j)` returns item j's digit (INVALID_DIGIT for padding items).
 template <int ITEMS, typename DigitAt>
 __device__ __forceinline__ void warp_rank_items(DigitAt digit_at, uint32_t (&rank)[ITEMS],
-                                                uint32_t *whist) {
+                                                uint32_t *whist, bool partial) {
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t lt = lanemask_lt();
 #pragma unroll
@@ -277,7 +328,11 @@ __device__ __forceinline__ void warp_rank_items(DigitAt digit_at, uint32_t (&ran
         for (int u = 0; u < G; ++u)
             if (g + u < ITEMS) {
                 d[u] = digit_at(g + u);
+#ifdef RSORT_RANK_MATCH_ANY
                 peers[u] = __match_any_sync(0xffffffffu, d[u]);
+#else
+                peers[u] = match_digit(d[u], partial);
+#endif
             }
 #pragma unroll
         for (int u = 0; u < G; ++u) {

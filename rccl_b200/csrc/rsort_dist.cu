@@ -234,7 +234,7 @@ cudaError_t merge_t(const MergeArgs &p, cudaStream_t s) {
     if (total == 0) return cudaSuccess;
     const uint64_t blocks = (total + MERGE_TILE - 1) / MERGE_TILE;
     auto k = merge_kernel<B, VB>;
-    if (S::BYTES > 48 * 1024) {
+    if (S::BYTES > 32 * 1024) {
         cudaError_t e =
             cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(S::BYTES));
         if (e != cudaSuccess) return e;
@@ -276,7 +276,7 @@ cudaError_t launch_splitters(const Composite *samples, uint32_t total, uint32_t 
     uint32_t np = 1;
     while (np < total) np <<= 1;
     const size_t bytes = size_t(np) * sizeof(Composite);
-    if (bytes > 48 * 1024) {
+    if (bytes > 32 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(splitters_kernel,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
         if (e != cudaSuccess) return e;

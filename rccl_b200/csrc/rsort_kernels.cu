@@ -171,7 +171,8 @@ struct OnesweepSmem {
     static constexpr int TILE = THREADS * ITEMS;
     static constexpr int VSIZE = VB > 0 ? VB : 1;
     static constexpr size_t WHIST = 0;
-    static constexpr size_t TSTART = WHIST + size_t(WARPS) * RADIX * 4;
+    static constexpr size_t WMASK = WHIST + size_t(WARPS) * RADIX * 4;
+    static constexpr size_t TSTART = WMASK + size_t(WARPS) * RADIX * 4;
     static constexpr size_t GBASE = TSTART + RADIX * 4;
     static constexpr size_t WSUMS = GBASE + RADIX * 8;
     static constexpr size_t CTL = WSUMS + 8 * 4;
@@ -187,6 +188,7 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, 2) onesweep_kernel(PassArgs 
     constexpr int THREADS = L::THREADS, WARPS = L::WARPS, TILE = L::TILE;
     extern __shared__ __align__(16) uint8_t smem[];
     uint32_t *whist = reinterpret_cast<uint32_t *>(smem + L::WHIST);
+    uint32_t *wmask = reinterpret_cast<uint32_t *>(smem + L::WMASK);
     uint32_t *tstart = reinterpret_cast<uint32_t *>(smem + L::TSTART);
     int64_t *gbase = reinterpret_cast<int64_t *>(smem + L::GBASE);
     uint32_t *wsums = reinterpret_cast<uint32_t *>(smem + L::WSUMS);
@@ -200,7 +202,7 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, 2) onesweep_kernel(PassArgs 
         ctl[0] = atomicAdd(a.tile_counter, 1);
         ctl[1] = 0;
     }
-    for (uint32_t i = tid; i < WARPS * RADIX; i += THREADS) whist[i] = 0;
+    for (uint32_t i = tid; i < 2 * WARPS * RADIX; i += THREADS) whist[i] = 0;  // + wmask
     __syncthreads();
 
     const int64_t tile = ctl[0];
@@ -240,12 +242,15 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, 2) onesweep_kernel(PassArgs 
 #pragma unroll
         for (int j = 0; j < ITEMS; ++j) key[j] = to_ordered_k<KIND>(key[j], dmask);
     }
-    warp_rank_items<ITEMS>(
-        [&](int j) {
-            return (full || seg + j * 32 + lane < count) ? digit_k<KIND>(key[j], a.shift, a.mask)
-                                                         : INVALID_DIGIT;
-        },
-        rank, whist + warp * RADIX);
+    auto digit_at = [&](int j) {
+        return (full || seg + j * 32 + lane < count) ? digit_k<KIND>(key[j], a.shift, a.mask)
+                                                     : INVALID_DIGIT;
+    };
+#ifdef RSORT_RANK_BALLOT
+    warp_rank_items<ITEMS>(digit_at, rank, whist + warp * RADIX, !full);
+#else
+    warp_rank_items_or<ITEMS>(digit_at, rank, whist + warp * RADIX, wmask + warp * RADIX);
+#endif
     __syncthreads();
 
     // 3. Per-digit tile totals -> look-back aggregate, warp offsets, tile scan.
@@ -383,7 +388,7 @@ __global__ void __launch_bounds__(SINGLE_THREADS, 1) single_tile_kernel(SingleAr
             if (a.desc) d = mask - d;
             dig[j] = pos < n ? d : INVALID_DIGIT;
         }
-        warp_rank_items<ITEMS>([&](int j) { return dig[j]; }, rank, whist + warp * RADIX);
+        warp_rank_items<ITEMS>([&](int j) { return dig[j]; }, rank, whist + warp * RADIX, true);
         __syncthreads();
         uint32_t total = 0;
         if (tid < RADIX) {
@@ -439,7 +444,7 @@ template <typename Kernel>
 cudaError_t ensure_smem(Kernel k, size_t bytes) {
     // cudaFuncSetAttribute is per function and device; calling it each launch
     // is cheap next to a sort and keeps the launcher stateless.
-    if (bytes <= 48 * 1024) return cudaSuccess;
+    if (bytes <= 32 * 1024) return cudaSuccess;
     return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
 }
 

@@ -17,8 +17,9 @@ constexpr int ONESWEEP_THREADS = 512;
 
 constexpr int onesweep_items(int key_bytes, int value_bytes) {
     return value_bytes == 0 ? (key_bytes == 4 ? 16 : 8)
-         : value_bytes == 16 ? 6
+         : value_bytes == 16 ? (key_bytes == 4 ? 6 : 4)
          : key_bytes == 4 ? (value_bytes <= 4 ? 12 : 8)
+         : value_bytes == 8 ? 7
          : 8;
 }
 
