@@ -306,7 +306,13 @@ __device__ __forceinline__ void warp_rank_items_or(DigitAt digit_at, uint32_t (&
         const uint32_t leader = 31 - __clz(peers);
         uint32_t got = 0;
         if (valid && lane == leader) {
+#ifdef RSORT_WHIST16
+            // two 16-bit counters per word (a warp's count never exceeds 2^16)
+            const uint32_t sh = (d & 1u) * 16u;
+            got = (atomicAdd(&whist[d >> 1], __popc(peers) << sh) >> sh) & 0xffffu;
+#else
             got = atomicAdd(&whist[d], __popc(peers));
+#endif
             wmask[d] = 0;
         }
         rank[j] = __shfl_sync(0xffffffffu, got, leader & 31) + __popc(peers & lt);

@@ -164,6 +164,15 @@ __global__ void __launch_bounds__(HIST_THREADS) histogram_kernel(HistArgs a) {
 //     (the last pass applies the ordered->raw transform)
 //  5. pairs: values follow through the same shared-memory permutation
 // ---------------------------------------------------------------------------
+#ifndef RSORT_MIN_BLOCKS
+#define RSORT_MIN_BLOCKS 2
+#endif
+#ifdef RSORT_WHIST16
+constexpr int WHIST_WORDS = RADIX / 2;
+#else
+constexpr int WHIST_WORDS = RADIX;
+#endif
+
 template <typename B, int VB, int ITEMS>
 struct OnesweepSmem {
     static constexpr int THREADS = ONESWEEP_THREADS;
@@ -171,7 +180,7 @@ struct OnesweepSmem {
     static constexpr int TILE = THREADS * ITEMS;
     static constexpr int VSIZE = VB > 0 ? VB : 1;
     static constexpr size_t WHIST = 0;
-    static constexpr size_t WMASK = WHIST + size_t(WARPS) * RADIX * 4;
+    static constexpr size_t WMASK = WHIST + size_t(WARPS) * WHIST_WORDS * 4;
     static constexpr size_t TSTART = WMASK + size_t(WARPS) * RADIX * 4;
     static constexpr size_t GBASE = TSTART + RADIX * 4;
     static constexpr size_t WSUMS = GBASE + RADIX * 8;
@@ -182,7 +191,7 @@ struct OnesweepSmem {
 };
 
 template <typename B, int VB, int ITEMS, int KIND>
-__global__ void __launch_bounds__(ONESWEEP_THREADS, 2) onesweep_kernel(PassArgs a) {
+__global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_kernel(PassArgs a) {
     using L = OnesweepSmem<B, VB, ITEMS>;
     using VT = typename ValueType<VB>::type;
     constexpr int THREADS = L::THREADS, WARPS = L::WARPS, TILE = L::TILE;
@@ -202,7 +211,7 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, 2) onesweep_kernel(PassArgs 
         ctl[0] = atomicAdd(a.tile_counter, 1);
         ctl[1] = 0;
     }
-    for (uint32_t i = tid; i < 2 * WARPS * RADIX; i += THREADS) whist[i] = 0;  // + wmask
+    for (uint32_t i = tid; i < WARPS * (WHIST_WORDS + RADIX); i += THREADS) whist[i] = 0;  // + wmask
     __syncthreads();
 
     const int64_t tile = ctl[0];
@@ -249,7 +258,7 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, 2) onesweep_kernel(PassArgs 
 #ifdef RSORT_RANK_BALLOT
     warp_rank_items<ITEMS>(digit_at, rank, whist + warp * RADIX, !full);
 #else
-    warp_rank_items_or<ITEMS>(digit_at, rank, whist + warp * RADIX, wmask + warp * RADIX);
+    warp_rank_items_or<ITEMS>(digit_at, rank, whist + warp * WHIST_WORDS, wmask + warp * RADIX);
 #endif
     __syncthreads();
 
@@ -257,12 +266,22 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, 2) onesweep_kernel(PassArgs 
     uint32_t total = 0;
     uint64_t *my_lb = a.lookback + uint64_t(tile) * RADIX + tid;
     if (tid < RADIX) {
+#ifdef RSORT_WHIST16
+        uint16_t *wh16 = reinterpret_cast<uint16_t *>(whist);
+#pragma unroll 4
+        for (int w = 0; w < WARPS; ++w) {
+            const uint32_t t = wh16[w * RADIX + tid];
+            wh16[w * RADIX + tid] = uint16_t(total);
+            total += t;
+        }
+#else
 #pragma unroll 4
         for (int w = 0; w < WARPS; ++w) {
             const uint32_t t = whist[w * RADIX + tid];
             whist[w * RADIX + tid] = total;
             total += t;
         }
+#endif
         st_relaxed_gpu(my_lb, lb_word(tile == 0 ? LB_INCLUSIVE : LB_AGGREGATE, a.tag, total));
     }
     const uint32_t tile_excl = block_exclusive_scan_256(total, wsums, nullptr);
@@ -278,7 +297,12 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, 2) onesweep_kernel(PassArgs 
         const uint32_t pos = seg + j * 32 + lane;
         if (full || pos < count) {
             const uint32_t d = digit_k<KIND>(key[j], a.shift, a.mask);
+#ifdef RSORT_WHIST16
+            const uint32_t r = tstart[d] +
+                               reinterpret_cast<const uint16_t *>(whist)[warp * RADIX + d] + rank[j];
+#else
             const uint32_t r = tstart[d] + whist[warp * RADIX + d] + rank[j];
+#endif
             if (r < count) {
                 skey[r] = key[j];
                 if constexpr (VB > 0) sval[r] = val[j];

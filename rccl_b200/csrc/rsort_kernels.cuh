@@ -13,7 +13,10 @@ namespace rsort {
 // 512-thread CTAs per SM), not the reference's Policy800 constants; only the
 // single-tile routing threshold keeps Policy800's value because it decides an
 // observable DoubleBuffer selector outcome.
-constexpr int ONESWEEP_THREADS = 512;
+#ifndef RSORT_ONESWEEP_THREADS
+#define RSORT_ONESWEEP_THREADS 512
+#endif
+constexpr int ONESWEEP_THREADS = RSORT_ONESWEEP_THREADS;
 
 constexpr int onesweep_items(int key_bytes, int value_bytes) {
     return value_bytes == 0 ? (key_bytes == 4 ? 16 : 8)
