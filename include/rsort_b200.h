@@ -181,6 +181,31 @@ rsort_status rsort_merge_runs(rsort_key_t key, int descending, void *keys, void 
                               void *scratch_keys, void *scratch_values, int *result_in_scratch,
                               rsort_stream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * Allocation-free keys sort (no reference counterpart).
+ *
+ * For callers that cannot allocate device memory where they sort: code
+ * recording a CUDA graph by stream capture (cudaMalloc is not allowed while
+ * capturing), plugins whose host framework owns every device byte through its
+ * own pool, and latency-critical loops that cannot take an allocation.  Same
+ * result as rsort_keys (in-place, full width, either direction, all six key
+ * types), but every scratch byte comes from one static device array inside
+ * the library instead of the caller.
+ *
+ * Limits: n <= RSORT_STATIC_MAX_ITEMS, else RSORT_WORKSPACE_TOO_SMALL.  The
+ * array (RSORT_STATIC_SCRATCH_BYTES) is held by every GPU that loads the
+ * library until exit.  All calls on a device share it, so calls whose work
+ * overlaps on the GPU race and must be serialized by the caller.  The first
+ * call on each device resolves the array's address; make it before any stream
+ * capture starts.  A bounded device wait that gives up is not reported here
+ * (the output is then unspecified).
+ * ------------------------------------------------------------------------- */
+#define RSORT_STATIC_MAX_ITEMS ((size_t)1 << 20)
+#define RSORT_STATIC_SCRATCH_BYTES ((size_t)9 << 20)
+
+rsort_status rsort_keys_static(rsort_key_t key, int descending, void *d_keys, size_t n,
+                               rsort_stream_t stream);
+
 const char *rsort_status_string(rsort_status status);
 void rsort_last_error(rsort_error_info *out);
 

@@ -50,6 +50,7 @@ EXPORTED_SYMBOLS = (
     "rsort_dist_bounds",
     "rsort_merge",
     "rsort_merge_runs",
+    "rsort_keys_static",
 )
 
 
@@ -111,6 +112,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.rsort_merge.restype = i
     lib.rsort_merge_runs.argtypes = [i, i, vp, vp, sz, ctypes.POINTER(sz), u, vp, vp, pi, vp]
     lib.rsort_merge_runs.restype = i
+    lib.rsort_keys_static.argtypes = [i, i, vp, sz, vp]
+    lib.rsort_keys_static.restype = i
 
 
 def lib() -> ctypes.CDLL:
