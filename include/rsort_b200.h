@@ -167,19 +167,24 @@ rsort_status rsort_dist_bounds(rsort_key_t key, int descending, const void *d_so
                                size_t m, unsigned rank, const void *d_splitters, unsigned world,
                                uint64_t *d_bounds, rsort_stream_t stream);
 
-/* Stable merge of two sorted runs (a then b; equal keys keep a first). */
+/* uint64 words of merge-path partition scratch a merge of `total` items needs. */
+size_t rsort_merge_partition_words(size_t total);
+
+/* Stable merge of two sorted runs (a then b; equal keys keep a first).
+ * d_partitions: caller scratch of rsort_merge_partition_words(na + nb) words. */
 rsort_status rsort_merge(rsort_key_t key, int descending, const void *a_keys,
                          const void *a_values, size_t na, const void *b_keys, const void *b_values,
                          size_t nb, void *out_keys, void *out_values, size_t value_bytes,
-                         rsort_stream_t stream);
+                         uint64_t *d_partitions, size_t npartitions, rsort_stream_t stream);
 
 /* Stable merge of `runs` consecutive sorted runs held in keys/values
  * (run_lengths is a host array).  The result is in keys/values, or in the
- * scratch buffers when *result_in_scratch is set on return. */
+ * scratch buffers when *result_in_scratch is set on return.  d_partitions
+ * needs rsort_merge_partition_words(total items) words. */
 rsort_status rsort_merge_runs(rsort_key_t key, int descending, void *keys, void *values,
                               size_t value_bytes, const size_t *run_lengths, unsigned runs,
-                              void *scratch_keys, void *scratch_values, int *result_in_scratch,
-                              rsort_stream_t stream);
+                              void *scratch_keys, void *scratch_values, uint64_t *d_partitions,
+                              size_t npartitions, int *result_in_scratch, rsort_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * Allocation-free keys sort (no reference counterpart).

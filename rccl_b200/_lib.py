@@ -48,6 +48,7 @@ EXPORTED_SYMBOLS = (
     "rsort_dist_samples",
     "rsort_dist_splitters",
     "rsort_dist_bounds",
+    "rsort_merge_partition_words",
     "rsort_merge",
     "rsort_merge_runs",
     "rsort_keys_static",
@@ -108,9 +109,12 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.rsort_dist_splitters.restype = i
     lib.rsort_dist_bounds.argtypes = [i, i, vp, sz, u, vp, u, vp, vp]
     lib.rsort_dist_bounds.restype = i
-    lib.rsort_merge.argtypes = [i, i, vp, vp, sz, vp, vp, sz, vp, vp, sz, vp]
+    lib.rsort_merge_partition_words.argtypes = [sz]
+    lib.rsort_merge_partition_words.restype = sz
+    lib.rsort_merge.argtypes = [i, i, vp, vp, sz, vp, vp, sz, vp, vp, sz, vp, sz, vp]
     lib.rsort_merge.restype = i
-    lib.rsort_merge_runs.argtypes = [i, i, vp, vp, sz, ctypes.POINTER(sz), u, vp, vp, pi, vp]
+    lib.rsort_merge_runs.argtypes = [i, i, vp, vp, sz, ctypes.POINTER(sz), u, vp, vp, vp, sz, pi,
+                                     vp]
     lib.rsort_merge_runs.restype = i
     lib.rsort_keys_static.argtypes = [i, i, vp, sz, vp]
     lib.rsort_keys_static.restype = i

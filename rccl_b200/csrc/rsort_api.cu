@@ -497,17 +497,22 @@ rsort_status rsort_dist_bounds(rsort_key_t key, int descending, const void *d_so
     return e == cudaSuccess ? RSORT_OK : cuda_fail(e, "bounds launch");
 }
 
+size_t rsort_merge_partition_words(size_t total) { return merge_partition_words(total, 0); }
+
 rsort_status rsort_merge(rsort_key_t key, int descending, const void *a_keys,
                          const void *a_values, size_t na, const void *b_keys, const void *b_values,
                          size_t nb, void *out_keys, void *out_values, size_t value_bytes,
-                         rsort_stream_t stream) {
+                         uint64_t *d_partitions, size_t npartitions, rsort_stream_t stream) {
     if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
     if (!value_ok(value_bytes)) return fail(RSORT_BAD_ARGUMENT, "radix value width");
     if (na + nb == 0) return RSORT_OK;
     if (!out_keys || (na && !a_keys) || (nb && !b_keys) ||
         (value_bytes && (!out_values || (na && !a_values) || (nb && !b_values))))
         return fail(RSORT_BAD_ARGUMENT, "null buffer");
-    if ((na + nb + 2047) / 2048 > 0x7fffffffull) return fail(RSORT_SIZE_OVERFLOW, "merge tiles");
+    if (merge_partition_words(na, nb) > 0x7fffffffull) return fail(RSORT_SIZE_OVERFLOW, "merge tiles");
+    if (!d_partitions || npartitions < merge_partition_words(na, nb))
+        return fail(RSORT_WORKSPACE_TOO_SMALL, "merge partitions", merge_partition_words(na, nb),
+                    npartitions);
     DeviceInfo dev;
     rsort_status st = device_info(&dev);
     if (st != RSORT_OK) return st;
@@ -517,15 +522,15 @@ rsort_status rsort_merge(rsort_key_t key, int descending, const void *a_keys,
     cudaError_t e;
     {
         LaunchScope scope(RSORT_KERNEL_MERGE, s);
-        e = launch_merge(key_bytes(key), int(value_bytes), p, s);
+        e = launch_merge(key_bytes(key), int(value_bytes), p, d_partitions, s);
     }
     return e == cudaSuccess ? RSORT_OK : cuda_fail(e, "merge launch");
 }
 
 rsort_status rsort_merge_runs(rsort_key_t key, int descending, void *keys, void *values,
                               size_t value_bytes, const size_t *run_lengths, unsigned runs,
-                              void *scratch_keys, void *scratch_values, int *result_in_scratch,
-                              rsort_stream_t stream) {
+                              void *scratch_keys, void *scratch_values, uint64_t *d_partitions,
+                              size_t npartitions, int *result_in_scratch, rsort_stream_t stream) {
     if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
     if (!value_ok(value_bytes)) return fail(RSORT_BAD_ARGUMENT, "radix value width");
     if (!result_in_scratch || (runs && !run_lengths)) return fail(RSORT_BAD_ARGUMENT, "null argument");
@@ -551,7 +556,7 @@ rsort_status rsort_merge_runs(rsort_key_t key, int descending, void *keys, void 
                     len[r], src_k + off[r + 1] * kb,
                     value_bytes ? src_v + off[r + 1] * value_bytes : nullptr, len[r + 1],
                     dst_k + off[r] * kb, value_bytes ? dst_v + off[r] * value_bytes : nullptr,
-                    value_bytes, stream);
+                    value_bytes, d_partitions, npartitions, stream);
                 if (st != RSORT_OK) return st;
                 nlen.push_back(len[r] + len[r + 1]);
             } else {

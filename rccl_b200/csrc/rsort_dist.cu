@@ -115,7 +115,7 @@ __global__ void bounds_kernel(const B *keys, uint64_t m, uint32_t rank, const Co
 // merges MERGE_ITEMS outputs per thread and writes the tile out coalesced.
 // ---------------------------------------------------------------------------
 constexpr int MERGE_THREADS = 256;
-constexpr int MERGE_ITEMS = 8;
+constexpr int MERGE_ITEMS = 16;
 constexpr int MERGE_TILE = MERGE_THREADS * MERGE_ITEMS;
 
 template <typename B>
@@ -133,14 +133,24 @@ __device__ __forceinline__ uint64_t merge_path(const B *a, uint64_t na, const B 
     return lo;
 }
 
+// Merge-path partitions: split[i] = number of A items among the first
+// i * MERGE_TILE outputs (one thread per tile boundary).
+template <typename B>
+__global__ void merge_partition_kernel(MergeArgs p, uint64_t *split, uint64_t nsplit) {
+    const uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= nsplit) return;
+    const uint64_t total = p.na + p.nb;
+    const uint64_t diag = i * MERGE_TILE < total ? i * MERGE_TILE : total;
+    split[i] = merge_path(static_cast<const B *>(p.a_keys), p.na, static_cast<const B *>(p.b_keys),
+                          p.nb, diag, KeyXform{p.kind, p.desc});
+}
+
 template <typename B, int VB>
 struct MergeSmem {
     static constexpr int VSIZE = VB > 0 ? VB : 1;
     static constexpr size_t KEYS = 0;                                  // A then B segment
     static constexpr size_t VALS = KEYS + size_t(MERGE_TILE) * sizeof(B);
-    static constexpr size_t OKEYS = VALS + (VB > 0 ? size_t(MERGE_TILE) * VSIZE : 0);
-    static constexpr size_t OVALS = OKEYS + size_t(MERGE_TILE) * sizeof(B);
-    static constexpr size_t BYTES = OVALS + (VB > 0 ? size_t(MERGE_TILE) * VSIZE : 0);
+    static constexpr size_t BYTES = VALS + (VB > 0 ? size_t(MERGE_TILE) * VSIZE : 0);
 };
 
 template <int VB> struct MergeValue;
@@ -151,16 +161,17 @@ template <> struct MergeValue<4> { using type = uint32_t; };
 template <> struct MergeValue<8> { using type = uint64_t; };
 template <> struct MergeValue<16> { using type = uint4; };
 
+// One CTA per MERGE_TILE outputs: stage the A and B segments given by the
+// precomputed partitions, let every thread merge MERGE_ITEMS outputs from its
+// own merge-path split, gather through shared memory and write the tile out
+// coalesced.
 template <typename B, int VB>
-__global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(MergeArgs p) {
+__global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(MergeArgs p, const uint64_t *split) {
     using S = MergeSmem<B, VB>;
     using VT = typename MergeValue<VB>::type;
     extern __shared__ __align__(16) uint8_t smem[];
     B *sk = reinterpret_cast<B *>(smem + S::KEYS);
     VT *sv = reinterpret_cast<VT *>(smem + S::VALS);
-    B *ok = reinterpret_cast<B *>(smem + S::OKEYS);
-    VT *ov = reinterpret_cast<VT *>(smem + S::OVALS);
-    __shared__ uint64_t split[2];
     const KeyXform xf{p.kind, p.desc};
     const B *ak = static_cast<const B *>(p.a_keys);
     const B *bk = static_cast<const B *>(p.b_keys);
@@ -169,13 +180,11 @@ __global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(MergeArgs p) {
     const uint64_t total = p.na + p.nb;
     const uint64_t d0 = uint64_t(blockIdx.x) * MERGE_TILE;
     const uint64_t d1 = d0 + MERGE_TILE < total ? d0 + MERGE_TILE : total;
-    if (threadIdx.x < 2)
-        split[threadIdx.x] = merge_path(ak, p.na, bk, p.nb, threadIdx.x == 0 ? d0 : d1, xf);
-    __syncthreads();
-    const uint64_t a0 = split[0], a1 = split[1];
+    const uint64_t a0 = split[blockIdx.x], a1 = split[blockIdx.x + 1];
     const uint64_t b0 = d0 - a0, b1 = d1 - a1;
     const uint32_t la = uint32_t(a1 - a0), lb = uint32_t(b1 - b0);
-    for (uint32_t i = threadIdx.x; i < la + lb; i += MERGE_THREADS) {
+    const uint32_t n = la + lb;
+    for (uint32_t i = threadIdx.x; i < n; i += MERGE_THREADS) {
         if (i < la) {
             sk[i] = ak[a0 + i];
             if constexpr (VB > 0) sv[i] = av[a0 + i];
@@ -185,10 +194,8 @@ __global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(MergeArgs p) {
         }
     }
     __syncthreads();
-    // Per-thread merge path inside the staged tile.
     const B *ta = sk;
     const B *tb = sk + la;
-    const uint32_t n = la + lb;
     const uint32_t diag = min(uint32_t(threadIdx.x) * MERGE_ITEMS, n);
     uint32_t lo = diag > lb ? diag - lb : 0, hi = diag < la ? diag : la;
     while (lo < hi) {
@@ -199,26 +206,40 @@ __global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(MergeArgs p) {
             hi = mid;
     }
     uint32_t ia = lo, ib = diag - lo;
+    B ok[MERGE_ITEMS];
+    VT ov[VB > 0 ? MERGE_ITEMS : 1];
+    uint64_t ima = ia < la ? image_of(ta[ia], xf) : 0;
+    uint64_t imb = ib < lb ? image_of(tb[ib], xf) : 0;
 #pragma unroll
     for (int k = 0; k < MERGE_ITEMS; ++k) {
-        const uint32_t o = diag + k;
-        if (o < n) {
-            bool take_a;
-            if (ia >= la) take_a = false;
-            else if (ib >= lb) take_a = true;
-            else take_a = image_of(ta[ia], xf) <= image_of(tb[ib], xf);
-            const uint32_t src = take_a ? ia : la + ib;
-            ok[o] = sk[src];
-            if constexpr (VB > 0) ov[o] = sv[src];
-            if (take_a) ++ia; else ++ib;
+        const bool take_a = ib >= lb || (ia < la && ima <= imb);
+        const uint32_t src = take_a ? ia : la + ib;
+        if (diag + k < n) {
+            ok[k] = sk[src];
+            if constexpr (VB > 0) ov[k] = sv[src];
+        }
+        if (take_a) {
+            ++ia;
+            if (ia < la) ima = image_of(ta[ia], xf);
+        } else {
+            ++ib;
+            if (ib < lb) imb = image_of(tb[ib], xf);
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < MERGE_ITEMS; ++k) {
+        if (diag + k < n) {
+            sk[diag + k] = ok[k];
+            if constexpr (VB > 0) sv[diag + k] = ov[k];
         }
     }
     __syncthreads();
     B *outk = static_cast<B *>(p.out_keys) + d0;
     VT *outv = static_cast<VT *>(p.out_values) + d0;
     for (uint32_t i = threadIdx.x; i < n; i += MERGE_THREADS) {
-        outk[i] = ok[i];
-        if constexpr (VB > 0) outv[i] = ov[i];
+        outk[i] = sk[i];
+        if constexpr (VB > 0) outv[i] = sv[i];
     }
 }
 
@@ -228,30 +249,33 @@ __global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(MergeArgs p) {
 namespace {
 
 template <typename B, int VB>
-cudaError_t merge_t(const MergeArgs &p, cudaStream_t s) {
+cudaError_t merge_t(const MergeArgs &p, uint64_t *split, cudaStream_t s) {
     using S = MergeSmem<B, VB>;
     const uint64_t total = p.na + p.nb;
     if (total == 0) return cudaSuccess;
     const uint64_t blocks = (total + MERGE_TILE - 1) / MERGE_TILE;
+    const uint64_t nsplit = blocks + 1;
+    merge_partition_kernel<B><<<dim3(uint32_t((nsplit + 255) / 256)), 256, 0, s>>>(p, split, nsplit);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
     auto k = merge_kernel<B, VB>;
     if (S::BYTES > 32 * 1024) {
-        cudaError_t e =
-            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(S::BYTES));
+        e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(S::BYTES));
         if (e != cudaSuccess) return e;
     }
-    k<<<dim3(uint32_t(blocks)), MERGE_THREADS, S::BYTES, s>>>(p);
+    k<<<dim3(uint32_t(blocks)), MERGE_THREADS, S::BYTES, s>>>(p, split);
     return cudaGetLastError();
 }
 
 template <typename B>
-cudaError_t merge_vb(int vb, const MergeArgs &p, cudaStream_t s) {
+cudaError_t merge_vb(int vb, const MergeArgs &p, uint64_t *split, cudaStream_t s) {
     switch (vb) {
-        case 0: return merge_t<B, 0>(p, s);
-        case 1: return merge_t<B, 1>(p, s);
-        case 2: return merge_t<B, 2>(p, s);
-        case 4: return merge_t<B, 4>(p, s);
-        case 8: return merge_t<B, 8>(p, s);
-        case 16: return merge_t<B, 16>(p, s);
+        case 0: return merge_t<B, 0>(p, split, s);
+        case 1: return merge_t<B, 1>(p, split, s);
+        case 2: return merge_t<B, 2>(p, split, s);
+        case 4: return merge_t<B, 4>(p, split, s);
+        case 8: return merge_t<B, 8>(p, split, s);
+        case 16: return merge_t<B, 16>(p, split, s);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -298,9 +322,14 @@ cudaError_t launch_bounds(int key_bytes, const void *keys, uint64_t m, uint32_t 
     return cudaGetLastError();
 }
 
-cudaError_t launch_merge(int key_bytes, int value_bytes, const MergeArgs &p, cudaStream_t s) {
-    return key_bytes == 4 ? merge_vb<uint32_t>(value_bytes, p, s)
-                          : merge_vb<uint64_t>(value_bytes, p, s);
+size_t merge_partition_words(uint64_t na, uint64_t nb) {
+    return size_t((na + nb + MERGE_TILE - 1) / MERGE_TILE + 1);
+}
+
+cudaError_t launch_merge(int key_bytes, int value_bytes, const MergeArgs &p, uint64_t *split,
+                         cudaStream_t s) {
+    return key_bytes == 4 ? merge_vb<uint32_t>(value_bytes, p, split, s)
+                          : merge_vb<uint64_t>(value_bytes, p, split, s);
 }
 
 }  // namespace rsort

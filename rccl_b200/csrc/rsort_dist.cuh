@@ -39,6 +39,9 @@ cudaError_t launch_splitters(const Composite *samples, uint32_t total, uint32_t 
 cudaError_t launch_bounds(int key_bytes, const void *keys, uint64_t m, uint32_t rank,
                           const Composite *splitters, uint32_t world, KeyXform xf,
                           uint64_t *bounds, cudaStream_t s);
-cudaError_t launch_merge(int key_bytes, int value_bytes, const MergeArgs &p, cudaStream_t s);
+// Words of the merge-path partition array a merge of na + nb items needs.
+size_t merge_partition_words(uint64_t na, uint64_t nb);
+cudaError_t launch_merge(int key_bytes, int value_bytes, const MergeArgs &p, uint64_t *split,
+                         cudaStream_t s);
 
 }  // namespace rsort

@@ -18,8 +18,26 @@ namespace rsort {
 #endif
 constexpr int ONESWEEP_THREADS = RSORT_ONESWEEP_THREADS;
 
+// Items per thread, tuned on B200 (bigger tiles shorten the look-back chain;
+// beyond these the 64-register budget spills).
+#ifndef RSORT_ITEMS_KEYS32
+#define RSORT_ITEMS_KEYS32 24
+#endif
+#ifndef RSORT_ITEMS_KEYS64
+#define RSORT_ITEMS_KEYS64 12
+#endif
+#ifndef RSORT_ITEMS_PAIRS64_32
+#define RSORT_ITEMS_PAIRS64_32 10
+#endif
+#ifndef RSORT_ITEMS_PAIRS32_32
+#define RSORT_ITEMS_PAIRS32_32 16
+#endif
 constexpr int onesweep_items(int key_bytes, int value_bytes) {
-    return value_bytes == 0 ? (key_bytes == 4 ? 16 : 8)
+    return (value_bytes == 0 && key_bytes == 4) ? RSORT_ITEMS_KEYS32
+         : (value_bytes == 0 && key_bytes == 8) ? RSORT_ITEMS_KEYS64
+         : (value_bytes == 4 && key_bytes == 8) ? RSORT_ITEMS_PAIRS64_32
+         : (value_bytes == 4 && key_bytes == 4) ? RSORT_ITEMS_PAIRS32_32
+         : value_bytes == 0 ? (key_bytes == 4 ? 16 : 8)
          : value_bytes == 16 ? (key_bytes == 4 ? 6 : 4)
          : key_bytes == 4 ? (value_bytes <= 4 ? 12 : 8)
          : value_bytes == 8 ? 7

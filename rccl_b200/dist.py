@@ -98,13 +98,16 @@ class CudaLocalOps:
             return keys, values
         sk = torch.empty_like(keys)
         sv = torch.empty_like(values) if values is not None else None
+        nparts = _lib.lib().rsort_merge_partition_words(keys.numel())
+        parts = torch.empty(nparts, dtype=torch.int64, device=keys.device)
         lens = (ctypes.c_size_t * runs)(*[int(x) for x in run_lengths])
         in_scratch = ctypes.c_int(0)
         vb = 0 if values is None else value_bytes_of(values)
         raise_for(_lib.lib().rsort_merge_runs(
             key_code(keys.dtype), int(descending), keys.data_ptr(),
             None if values is None else values.data_ptr(), vb, lens, runs, sk.data_ptr(),
-            None if sv is None else sv.data_ptr(), ctypes.byref(in_scratch), self.launch.handle))
+            None if sv is None else sv.data_ptr(), parts.data_ptr(), nparts,
+            ctypes.byref(in_scratch), self.launch.handle))
         if in_scratch.value:
             return sk, sv
         return keys, values
@@ -161,22 +164,55 @@ def sample_sort(keys: torch.Tensor, values: Optional[torch.Tensor] = None,
     dist.all_to_all_single(recv, send, group=group)
     send_l, recv_l = send.tolist(), recv.tolist()
     ev.mark("partition")
-    kb = keys.element_size()
     out_k = torch.empty(sum(recv_l), dtype=keys.dtype, device=keys.device)
-    dist.all_to_all_single(_bytes(out_k), _bytes(keys), [c * kb for c in recv_l],
-                           [c * kb for c in send_l], group=group)
     out_v = None
     if values is not None:
-        vb = value_bytes_of(values)
         shape = (sum(recv_l),) + tuple(values.shape[1:])
         out_v = torch.empty(shape, dtype=values.dtype, device=values.device)
-        dist.all_to_all_single(_bytes(out_v), _bytes(values), [c * vb for c in recv_l],
-                               [c * vb for c in send_l], group=group)
+    exchange(keys, values, out_k, out_v, send_l, recv_l, rank, world, group)
     ev.mark("exchange")
     out = phase_merge(ops, out_k, out_v, recv_l, descending)
     ev.mark("merge")
     ev.finish()
     return out
+
+
+def exchange(keys, values, out_k, out_v, send_l, recv_l, rank: int, world: int, group=None):
+    """Bucket exchange: every (rank -> peer) key and value bucket in ONE group
+    of NCCL send/recv operations (torch.distributed.batch_isend_irecv), so
+    keys and values of all peers move concurrently; the bucket a rank keeps is
+    a local device copy."""
+    import torch.distributed as dist
+    kb = keys.element_size()
+    vb = value_bytes_of(values) if values is not None else 0
+    src_k, dst_k = _bytes(keys), _bytes(out_k)
+    src_v = _bytes(values) if values is not None else None
+    dst_v = _bytes(out_v) if values is not None else None
+    soff = [0] * (world + 1)
+    roff = [0] * (world + 1)
+    for q in range(world):
+        soff[q + 1] = soff[q] + send_l[q]
+        roff[q + 1] = roff[q] + recv_l[q]
+    ops = []
+    for q in range(world):
+        if q == rank:
+            continue
+        if send_l[q]:
+            ops.append(dist.P2POp(dist.isend, src_k[soff[q] * kb:soff[q + 1] * kb], q, group))
+            if vb:
+                ops.append(dist.P2POp(dist.isend, src_v[soff[q] * vb:soff[q + 1] * vb], q, group))
+        if recv_l[q]:
+            ops.append(dist.P2POp(dist.irecv, dst_k[roff[q] * kb:roff[q + 1] * kb], q, group))
+            if vb:
+                ops.append(dist.P2POp(dist.irecv, dst_v[roff[q] * vb:roff[q + 1] * vb], q, group))
+    if send_l[rank]:
+        dst_k[roff[rank] * kb:roff[rank + 1] * kb].copy_(src_k[soff[rank] * kb:soff[rank + 1] * kb])
+        if vb:
+            dst_v[roff[rank] * vb:roff[rank + 1] * vb].copy_(
+                src_v[soff[rank] * vb:soff[rank + 1] * vb])
+    if ops:
+        for req in dist.batch_isend_irecv(ops):
+            req.wait()
 
 
 class _Events:
