@@ -129,6 +129,13 @@ rsort_status rsort_pairs(rsort_key_t key, int descending, void *d_keys, void *d_
 rsort_status rsort_check_device_status(int32_t *counters, size_t ncounters,
                                        rsort_stream_t stream);
 
+/* Failure-detection self test (no reference counterpart).  Runs one onesweep
+ * CTA whose look-back waits on a predecessor that never publishes; the bounded
+ * wait (about one second) must give up.  Returns RSORT_TIMEOUT when it does
+ * (the expected result) and leaves the context usable.  Synchronizes
+ * `stream` and allocates its own small buffers (test hook, not a sort path). */
+rsort_status rsort_selftest_lookback_timeout(rsort_stream_t stream);
+
 /* Single-tile extent used for routing: identical to the reference's Policy800
  * threshold (rccl-cub/src/workspace.rs:43-66). */
 size_t rsort_single_tile_items(rsort_key_t key, size_t value_bytes);

@@ -52,6 +52,7 @@ EXPORTED_SYMBOLS = (
     "rsort_merge",
     "rsort_merge_runs",
     "rsort_keys_static",
+    "rsort_selftest_lookback_timeout",
 )
 
 
@@ -118,6 +119,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.rsort_merge_runs.restype = i
     lib.rsort_keys_static.argtypes = [i, i, vp, sz, vp]
     lib.rsort_keys_static.restype = i
+    lib.rsort_selftest_lookback_timeout.argtypes = [vp]
+    lib.rsort_selftest_lookback_timeout.restype = i
 
 
 def lib() -> ctypes.CDLL:

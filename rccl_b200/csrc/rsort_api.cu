@@ -583,6 +583,64 @@ rsort_status rsort_merge_runs(rsort_key_t key, int descending, void *keys, void 
     return RSORT_OK;
 }
 
+// Failure-detection self test: one onesweep CTA is handed tile 1 of a
+// two-tile input whose tile 0 is never processed, so its look-back waits on a
+// word nothing publishes.  The wait must give up within its bound, set the
+// status word and skip its writes; the call returns the status the host reads.
+rsort_status rsort_selftest_lookback_timeout(rsort_stream_t stream) {
+    DeviceInfo dev;
+    rsort_status st = device_info(&dev);
+    if (st != RSORT_OK) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const size_t tile = size_t(onesweep_tile(4, 0));
+    const size_t n = 2 * tile;
+    uint32_t *keys = nullptr, *out = nullptr;
+    uint64_t *bins = nullptr, *lookback = nullptr;
+    int32_t *counters = nullptr;
+    cudaError_t e = cudaMalloc(&keys, n * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&out, n * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&bins, RADIX * 8);
+    if (e == cudaSuccess) e = cudaMalloc(&lookback, 2 * RADIX * 8);
+    if (e == cudaSuccess) e = cudaMalloc(&counters, CTR_WORDS * 4);
+    if (e == cudaSuccess) e = cudaMemsetAsync(keys, 0, n * 4, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(out, 0, n * 4, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(bins, 0, RADIX * 8, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(lookback, 0, 2 * RADIX * 8, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(counters, 0, CTR_WORDS * 4, s);
+    const int32_t one = 1;  // the single CTA claims tile 1
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(counters + CTR_TILE, &one, sizeof(one), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) {
+        PassArgs a{};
+        a.keys_in = keys;
+        a.keys_out = out;
+        a.n = n;
+        a.bins = bins;
+        a.lookback = lookback;
+        a.tile_counter = counters + CTR_TILE;
+        a.status = counters + CTR_STATUS;
+        a.shift = 0;
+        a.mask = 0xff;
+        a.kind = KIND_UINT;
+        a.first = 1;
+        a.last = 1;
+        a.tag = 1;
+        e = launch_onesweep(4, 0, a, 1, s);
+    }
+    int32_t word = 0;
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(&word, counters + CTR_STATUS, sizeof(word), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    cudaFree(keys);
+    cudaFree(out);
+    cudaFree(bins);
+    cudaFree(lookback);
+    cudaFree(counters);
+    if (e != cudaSuccess) return cuda_fail(e, "self test");
+    if (word == DEV_STATUS_TIMEOUT) return fail(RSORT_TIMEOUT, "radix look-back wait (self test)");
+    return word == 0 ? RSORT_OK : fail(RSORT_CUDA_ERROR, "radix scatter bounds check");
+}
+
 void rsort_profile_enable(int enable) { g_profile = enable != 0; }
 
 size_t rsort_profile_read(int32_t *kernel_ids, float *milliseconds, size_t capacity) {

@@ -180,9 +180,17 @@ __device__ __forceinline__ uint64_t lb_word(uint64_t state, uint32_t tag, uint64
 // one or two round trips.
 constexpr int LOOKBACK_WINDOW = 16;
 
-// Iteration bound of one look-back wait: with the back-off below this is
-// roughly a second of wall time before the wait gives up.
-constexpr uint32_t LOOKBACK_SPIN_LIMIT = 1u << 22;
+// Bound of one look-back wait: it gives up after LOOKBACK_TIMEOUT_NS of wall
+// time (device %globaltimer), or after LOOKBACK_SPIN_LIMIT polls, whichever
+// comes first.
+constexpr uint64_t LOOKBACK_TIMEOUT_NS = 1000000000ull;
+constexpr uint32_t LOOKBACK_SPIN_LIMIT = 1u << 24;
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 // Sums the per-digit counts of all tiles before `tile`: walks back in windows
 // of LOOKBACK_WINDOW predecessors, adding aggregates until it meets an
@@ -195,6 +203,7 @@ __device__ __forceinline__ uint64_t lookback_exclusive(const uint64_t *lookback,
     uint64_t exclusive = 0;
     int64_t t = tile - 1;
     uint32_t spins = 0;
+    uint64_t wait_start = 0;
     const uint32_t want_tag = tag & 0x3fff;
     while (t >= 0) {
         uint64_t w[LOOKBACK_WINDOW];
@@ -232,11 +241,19 @@ __device__ __forceinline__ uint64_t lookback_exclusive(const uint64_t *lookback,
                 --t;
                 break;
             }
+            if (spins == 0) wait_start = global_ns();
             ++spins;
             if (spins > 8) __nanosleep(spins > 4096 ? 256 : 32);
-            if ((spins & 255) == 0 && ld_relaxed_gpu(status) != 0) {
-                *gave_up = true;
-                return exclusive;
+            if ((spins & 255) == 0) {
+                if (ld_relaxed_gpu(status) != 0) {
+                    *gave_up = true;
+                    return exclusive;
+                }
+                if (global_ns() - wait_start > LOOKBACK_TIMEOUT_NS) {
+                    atomicExch(status, DEV_STATUS_TIMEOUT);
+                    *gave_up = true;
+                    return exclusive;
+                }
             }
             if (spins > LOOKBACK_SPIN_LIMIT) {
                 atomicExch(status, DEV_STATUS_TIMEOUT);
@@ -284,40 +301,69 @@ __device__ __forceinline__ uint32_t match_digit(uint32_t d, bool check_valid) {
     return peers;
 }
 
-// Peer masks through shared memory: every lane ORs its lane bit into the
-// warp's mask word of its digit, reads the word back after a warp barrier, and
-// the group leader clears it after a second barrier.  About a dozen
-// instructions per item (against ~30 for the ballot network) with no
-// ordering assumption beyond __syncwarp.  `wmask` is the warp's 256-word mask
-// array, all zero between uses.
+// Warp multi-split rank, one item per lane per step, steps in input order.
+// Per step the lanes of each digit find their peer group, the group's leader
+// (its highest lane) reads the warp's running count for the digit and stores
+// it back advanced by the group size with plain shared loads and stores (one
+// leader per digit per step, so no atomic is needed), and every lane takes
+// base + its rank among lower peers.  Shared atomics are slow on sm_100
+// (~6 lanes per clock per SM measured), so the peer search avoids them where
+// it can:
+//   RSORT_RANK_MODE 0: peers via a shared atomicOr of lane bits into the
+//                      warp's 256-word mask array (cleared by the leader)
+//   RSORT_RANK_MODE 1: owner election without atomics: every lane stores its
+//                      lane id to owner[d]; the surviving id names the group
+//                      and five ballots on its bits give the peer mask
+// `wmask` is the warp's 256-word scratch (mask array or owner array).
+#ifndef RSORT_RANK_MODE
+#define RSORT_RANK_MODE 0
+#endif
+
+__device__ __forceinline__ uint32_t match_lane_id(uint32_t w, bool valid) {
+    uint32_t peers = __ballot_sync(0xffffffffu, valid);
+    peers = valid ? peers : ~peers;
+#pragma unroll
+    for (int b = 0; b < 5; ++b) {
+        const bool set = (w >> b) & 1u;
+        const uint32_t v = __ballot_sync(0xffffffffu, set);
+        peers &= set ? v : ~v;
+    }
+    return peers;
+}
+
 template <int ITEMS, typename DigitAt>
 __device__ __forceinline__ void warp_rank_items_or(DigitAt digit_at, uint32_t (&rank)[ITEMS],
                                                    uint32_t *whist, uint32_t *wmask) {
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t lt = lanemask_lt(), bit = 1u << lane;
+    (void)bit;
 #pragma unroll
     for (int j = 0; j < ITEMS; ++j) {
         const uint32_t d = digit_at(j);
         const bool valid = d < RADIX;
+#if RSORT_RANK_MODE == 0
         if (valid) atomicOr(&wmask[d], bit);
         __syncwarp();
         const uint32_t peers = valid ? wmask[d] : 0u;
+#else
+        if (valid) wmask[d] = lane;
+        __syncwarp();
+        const uint32_t owner = valid ? wmask[d] : 0u;
+        const uint32_t peers = match_lane_id(owner, valid);
+#endif
         __syncwarp();
         const uint32_t leader = 31 - __clz(peers);
         uint32_t got = 0;
         if (valid && lane == leader) {
-#ifdef RSORT_WHIST16
-            // two 16-bit counters per word (a warp's count never exceeds 2^16)
-            const uint32_t sh = (d & 1u) * 16u;
-            got = (atomicAdd(&whist[d >> 1], __popc(peers) << sh) >> sh) & 0xffffu;
-#else
-            got = atomicAdd(&whist[d], __popc(peers));
-#endif
+            got = whist[d];
+            whist[d] = got + __popc(peers);
+#if RSORT_RANK_MODE == 0
             wmask[d] = 0;
+#endif
         }
+        __syncwarp();
         rank[j] = __shfl_sync(0xffffffffu, got, leader & 31) + __popc(peers & lt);
     }
-    __syncwarp();
 }
 
 // `digit_at(j)` returns item j's digit (INVALID_DIGIT for padding items).
