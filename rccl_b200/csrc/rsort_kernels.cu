@@ -31,10 +31,25 @@ __global__ void init_kernel(uint64_t *bins, uint32_t nbins, int *counters, uint3
 // Histogram of every digit pass in one read of the keys.  Also zeroes the
 // look-back words for the whole sort, and the last CTA to finish turns the
 // digit counts into global exclusive digit offsets (one scan per pass).
+//
+// Counter layout: one column of counters per lane (32 columns for 32-bit
+// keys, 16 for 64-bit keys), counter (pass, digit, column) at word
+// (pass * 256 + digit) * COLS + column.  Lane l of every warp adds into
+// column l % COLS, so the 32 lanes of one shared atomic hit 32 different
+// banks (64-bit keys: at most 2 lanes per bank) whatever the digits are: the
+// count runs at the shared-atomic issue rate, also on skewed inputs where a
+// single-copy histogram serializes on one address.  The 128 KB of counters
+// take the shared memory of one 1024-thread CTA per SM.
 // ---------------------------------------------------------------------------
-constexpr int HIST_THREADS = 512;
-constexpr int HIST_COPIES = 2;
+constexpr int HIST_THREADS = 1024;
 constexpr int HIST_UNROLL = 4;
+
+template <typename B> struct HistShape {
+    static constexpr int MAX_PASSES = int(sizeof(B));  // 8-bit digits
+    static constexpr int COLS = sizeof(B) == 4 ? 32 : 16;
+    static constexpr size_t WORDS = size_t(MAX_PASSES) * RADIX * COLS;
+    static constexpr size_t BYTES = WORDS * 4;
+};
 
 __device__ __forceinline__ uint64_t block_exclusive_scan_256_u64(uint64_t v, uint64_t *warp_sums) {
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -56,26 +71,43 @@ __device__ __forceinline__ uint64_t block_exclusive_scan_256_u64(uint64_t v, uin
     return prefix + inc - v;
 }
 
-template <typename B>
-__device__ __forceinline__ void hist_count(B raw, const HistArgs &a, uint32_t *h) {
-    const KeyXform xf{a.kind, a.desc};
-    const B o = to_ordered(raw, xf);
-#pragma unroll 1
-    for (uint32_t p = 0; p < a.passes; ++p) {
-        const uint32_t bit = a.begin_bit + 8 * p;
-        const uint32_t bits = min(8u, a.end_bit - bit);
-        const uint32_t d = digit_of(o, a.kind, bit, (1u << bits) - 1);
-        atomicAdd(&h[p * RADIX + d], 1u);
+// Counts one key into every pass's digit counters (column already applied to
+// `hc`).  FULL: the bit window is the whole key, so every shift is a
+// compile-time constant.
+template <typename B, int KIND, bool FULL>
+__device__ __forceinline__ void hist_count(B raw, B dmask, uint32_t passes, uint32_t begin_bit,
+                                           uint32_t last_mask, uint32_t *hc) {
+    using S = HistShape<B>;
+    using T = KeyBits<B>;
+    B o = to_ordered_k<KIND>(raw, dmask);
+    if constexpr (KIND == KIND_FLOAT) {
+        if (o == B(T::SIGN - 1)) o = B(T::SIGN);
+    }
+#pragma unroll
+    for (int p = 0; p < S::MAX_PASSES; ++p) {
+        uint32_t d;
+        if constexpr (FULL) {
+            d = uint32_t(o >> (8 * p)) & 0xffu;
+        } else {
+            if (uint32_t(p) >= passes) break;
+            const uint32_t mask = uint32_t(p) + 1 == passes ? last_mask : 0xffu;
+            d = uint32_t(o >> (begin_bit + 8 * p)) & mask;
+        }
+        atomicAdd(hc + (p * RADIX + d) * S::COLS, 1u);
     }
 }
 
-template <typename B>
-__global__ void __launch_bounds__(HIST_THREADS) histogram_kernel(HistArgs a) {
-    __shared__ uint32_t h[HIST_COPIES][8 * RADIX];
+template <typename B, int KIND, bool FULL>
+__global__ void __launch_bounds__(HIST_THREADS, 1) histogram_kernel(HistArgs a) {
+    using S = HistShape<B>;
+    extern __shared__ __align__(16) uint32_t h[];
     __shared__ uint64_t warp_sums[8];
     __shared__ int is_last;
-    const uint32_t tid = threadIdx.x;
-    for (uint32_t i = tid; i < HIST_COPIES * 8 * RADIX; i += HIST_THREADS) (&h[0][0])[i] = 0;
+    const uint32_t tid = threadIdx.x, lane = tid & 31;
+    {
+        uint4 *h4 = reinterpret_cast<uint4 *>(h);
+        for (uint32_t i = tid; i < S::WORDS / 4; i += HIST_THREADS) h4[i] = make_uint4(0, 0, 0, 0);
+    }
 
     // Zero this sort's look-back words (grid-stride, 16-byte stores).
     {
@@ -89,7 +121,14 @@ __global__ void __launch_bounds__(HIST_THREADS) histogram_kernel(HistArgs a) {
     }
     __syncthreads();
 
-    uint32_t *mine = h[(tid >> 5) % HIST_COPIES];
+    const B dmask = a.desc ? B(~B(0)) : B(0);
+    const uint32_t passes = a.passes, begin_bit = a.begin_bit;
+    const uint32_t last_bits = a.end_bit - (begin_bit + 8 * (passes - 1));
+    const uint32_t last_mask = (1u << last_bits) - 1;
+    uint32_t *hc = h + (lane % S::COLS);
+    auto count = [&](B raw) {
+        hist_count<B, KIND, FULL>(raw, dmask, passes, begin_bit, last_mask, hc);
+    };
     const uint64_t stride = uint64_t(gridDim.x) * HIST_THREADS;
     const uint64_t gtid = uint64_t(blockIdx.x) * HIST_THREADS + tid;
     const B *keys = static_cast<const B *>(a.keys);
@@ -112,25 +151,27 @@ __global__ void __launch_bounds__(HIST_THREADS) histogram_kernel(HistArgs a) {
             for (int u = 0; u < HIST_UNROLL; ++u) {
                 if (i + uint64_t(u) * stride >= nvec) break;
                 if constexpr (sizeof(B) == 4) {
-                    hist_count<B>(v[u].x, a, mine);
-                    hist_count<B>(v[u].y, a, mine);
-                    hist_count<B>(v[u].z, a, mine);
-                    hist_count<B>(v[u].w, a, mine);
+                    count(v[u].x);
+                    count(v[u].y);
+                    count(v[u].z);
+                    count(v[u].w);
                 } else {
-                    hist_count<B>((uint64_t(v[u].y) << 32) | v[u].x, a, mine);
-                    hist_count<B>((uint64_t(v[u].w) << 32) | v[u].z, a, mine);
+                    count((uint64_t(v[u].y) << 32) | v[u].x);
+                    count((uint64_t(v[u].w) << 32) | v[u].z);
                 }
             }
         }
         scalar_begin = nvec * PER;
     }
-    for (uint64_t i = scalar_begin + gtid; i < a.n; i += stride) hist_count<B>(keys[i], a, mine);
+    for (uint64_t i = scalar_begin + gtid; i < a.n; i += stride) count(keys[i]);
     __syncthreads();
 
-    for (uint32_t i = tid; i < a.passes * RADIX; i += HIST_THREADS) {
+    // Column sums; each lane starts at a different column so the reads of a
+    // warp spread over the banks.
+    for (uint32_t i = tid; i < passes * RADIX; i += HIST_THREADS) {
         uint32_t c = 0;
-#pragma unroll
-        for (int k = 0; k < HIST_COPIES; ++k) c += h[k][i];
+#pragma unroll 8
+        for (int k = 0; k < S::COLS; ++k) c += h[i * S::COLS + ((k + lane) % S::COLS)];
         if (c) atomicAdd(reinterpret_cast<unsigned long long *>(&a.bins[i]),
                          static_cast<unsigned long long>(c));
     }
@@ -529,13 +570,38 @@ cudaError_t launch_init(uint64_t *bins, size_t nbins, int *counters, size_t ncou
     return cudaGetLastError();
 }
 
-cudaError_t launch_histogram(int key_bytes, const HistArgs &a, int sm_count, cudaStream_t stream) {
-    const int blocks = sm_count * 2;
-    if (key_bytes == 4)
-        histogram_kernel<uint32_t><<<blocks, HIST_THREADS, 0, stream>>>(a);
-    else
-        histogram_kernel<uint64_t><<<blocks, HIST_THREADS, 0, stream>>>(a);
+template <typename B, int KIND, bool FULL>
+static cudaError_t histogram_launch(const HistArgs &a, int blocks, cudaStream_t stream) {
+    constexpr size_t smem = HistShape<B>::BYTES;
+    static_assert(smem + 256 <= 227 * 1024, "histogram shared memory");
+    cudaError_t e = cudaFuncSetAttribute(histogram_kernel<B, KIND, FULL>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    histogram_kernel<B, KIND, FULL><<<blocks, HIST_THREADS, smem, stream>>>(a);
     return cudaGetLastError();
+}
+
+template <typename B, int KIND>
+static cudaError_t histogram_full(const HistArgs &a, int blocks, cudaStream_t stream) {
+    const bool full = a.begin_bit == 0 && a.end_bit == 8 * sizeof(B);
+    return full ? histogram_launch<B, KIND, true>(a, blocks, stream)
+                : histogram_launch<B, KIND, false>(a, blocks, stream);
+}
+
+template <typename B>
+static cudaError_t histogram_kind(const HistArgs &a, int blocks, cudaStream_t stream) {
+    switch (a.kind) {
+        case KIND_SINT: return histogram_full<B, KIND_SINT>(a, blocks, stream);
+        case KIND_FLOAT: return histogram_full<B, KIND_FLOAT>(a, blocks, stream);
+        default: return histogram_full<B, KIND_UINT>(a, blocks, stream);
+    }
+}
+
+cudaError_t launch_histogram(int key_bytes, const HistArgs &a, int sm_count, cudaStream_t stream) {
+    // One 1024-thread CTA per SM (the counters fill the SM's shared memory).
+    const int blocks = sm_count;
+    return key_bytes == 4 ? histogram_kind<uint32_t>(a, blocks, stream)
+                          : histogram_kind<uint64_t>(a, blocks, stream);
 }
 
 cudaError_t launch_onesweep(int key_bytes, int value_bytes, const PassArgs &a, uint64_t tiles,
