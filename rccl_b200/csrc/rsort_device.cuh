@@ -314,10 +314,16 @@ __device__ __forceinline__ uint32_t match_digit(uint32_t d, bool check_valid) {
 //   RSORT_RANK_MODE 1: owner election without atomics: every lane stores its
 //                      lane id to owner[d]; the surviving id names the group
 //                      and five ballots on its bits give the peer mask
-// `wmask` is the warp's 256-word scratch (mask array or owner array).
+//   RSORT_RANK_MODE 2: as mode 0, with RANK_MASK_SETS mask arrays used in
+//                      rotation: item j ORs into set j % 3 and the leader of
+//                      item j clears its word while item j + 1 runs, after
+//                      the sync that orders it behind every read of it.  One
+//                      __syncwarp per item instead of three.
+// `wmask` is the warp's scratch (mask arrays or owner array).
 #ifndef RSORT_RANK_MODE
-#define RSORT_RANK_MODE 0
+#define RSORT_RANK_MODE 2
 #endif
+constexpr int RANK_MASK_SETS = RSORT_RANK_MODE == 2 ? 3 : 1;
 
 __device__ __forceinline__ uint32_t match_lane_id(uint32_t w, bool valid) {
     uint32_t peers = __ballot_sync(0xffffffffu, valid);
@@ -329,6 +335,46 @@ __device__ __forceinline__ uint32_t match_lane_id(uint32_t w, bool valid) {
         peers &= set ? v : ~v;
     }
     return peers;
+}
+
+// rank[j] = digit << 16 | rank of item j among the warp's items of its digit.
+// ALL_VALID: no padding items (full tile), so no per-item validity tests.
+template <int ITEMS, bool ALL_VALID, typename DigitAt>
+__device__ __forceinline__ void warp_rank_items_or3(DigitAt digit_at, uint32_t (&rank)[ITEMS],
+                                                    uint32_t *whist, uint32_t *wmask) {
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t lt = lanemask_lt(), bit = 1u << lane;
+    uint32_t prev_d = 0;
+    bool prev_leader = false;
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {
+        uint32_t *m = wmask + (j % 3) * RADIX;
+        const uint32_t d = digit_at(j);
+        const bool valid = ALL_VALID || d < RADIX;
+        if (valid) atomicOr(&m[d], bit);
+        // Orders this item's ORs before the reads below, the previous item's
+        // reads before its clear below, and the previous item's whist update
+        // before this item's whist read.
+        __syncwarp();
+        if (prev_leader) wmask[((j + 2) % 3) * RADIX + prev_d] = 0u;
+        const uint32_t peers = valid ? m[d] : 0u;
+        const uint32_t leader = 31 - __clz(peers);
+        const bool is_leader = valid && lane == leader;
+        uint32_t got = 0;
+        if (is_leader) {
+            got = whist[d];
+            whist[d] = got + __popc(peers);
+        }
+        prev_leader = is_leader;
+        prev_d = d;
+        // Packed (digit << 16 | rank): the rank within the warp is below
+        // 32 * ITEMS < 2^16, and the scatter reads the digit back from here.
+        rank[j] = (d << 16) | (__shfl_sync(0xffffffffu, got, leader & 31) + __popc(peers & lt));
+        asm volatile("" : "+r"(rank[j]));
+    }
+    // The last item's mask word stays set: the scratch is re-zeroed before
+    // the next tile uses it.
+    __syncwarp();
 }
 
 template <int ITEMS, typename DigitAt>

@@ -208,11 +208,10 @@ __global__ void __launch_bounds__(HIST_THREADS, 1) histogram_kernel(HistArgs a) 
 #ifndef RSORT_MIN_BLOCKS
 #define RSORT_MIN_BLOCKS 2
 #endif
-#ifdef RSORT_WHIST16
-constexpr int WHIST_WORDS = RADIX / 2;
-#else
-constexpr int WHIST_WORDS = RADIX;
+#ifndef RSORT_COMBINED_OFFSETS
+#define RSORT_COMBINED_OFFSETS 1
 #endif
+constexpr int WHIST_WORDS = RADIX;
 
 template <typename B, int VB, int ITEMS>
 struct OnesweepSmem {
@@ -220,22 +219,38 @@ struct OnesweepSmem {
     static constexpr int WARPS = THREADS / 32;
     static constexpr int TILE = THREADS * ITEMS;
     static constexpr int VSIZE = VB > 0 ? VB : 1;
+    // The rank-phase mask arrays (WMASK) and the scatter-phase key/value
+    // staging (KEYS, VALS) are never live at the same time: they share one
+    // region, separated by the __syncthreads after ranking.
     static constexpr size_t WHIST = 0;
-    static constexpr size_t WMASK = WHIST + size_t(WARPS) * WHIST_WORDS * 4;
-    static constexpr size_t TSTART = WMASK + size_t(WARPS) * RADIX * 4;
+    static constexpr size_t TSTART = WHIST + size_t(WARPS) * WHIST_WORDS * 4;
     static constexpr size_t GBASE = TSTART + RADIX * 4;
     static constexpr size_t WSUMS = GBASE + RADIX * 8;
     static constexpr size_t CTL = WSUMS + 8 * 4;
-    static constexpr size_t KEYS = (CTL + 16 + 15) / 16 * 16;
+    static constexpr size_t WMASK = (CTL + 16 + 15) / 16 * 16;
+    static constexpr size_t MASK_BYTES = size_t(WARPS) * RANK_MASK_SETS * RADIX * 4;
+    static constexpr size_t KEYS = WMASK;
     static constexpr size_t VALS = KEYS + size_t(TILE) * sizeof(B);
-    static constexpr size_t BYTES = VALS + (VB > 0 ? size_t(TILE) * VSIZE : 0);
+    static constexpr size_t STAGE_BYTES = size_t(TILE) * sizeof(B) + (VB > 0 ? size_t(TILE) * VSIZE : 0);
+    static constexpr size_t BYTES = WMASK + (MASK_BYTES > STAGE_BYTES ? MASK_BYTES : STAGE_BYTES);
 };
 
-template <typename B, int VB, int ITEMS, int KIND>
+template <bool V> struct BoolTag {
+    static constexpr bool value = V;
+};
+
+// PERSIST: a persistent grid whose CTAs claim tiles until none are left and
+// load the next tile while writing out the current one (measured faster for
+// 8-byte keys); otherwise one tile per CTA (faster for 4-byte keys, whose
+// tiles are larger).  The per-tile body is compiled twice, for full tiles
+// (no per-item bounds tests, fully unrolled write-out) and for the last,
+// partial tile.
+template <typename B, int VB, int ITEMS, int KIND, bool PERSIST>
 __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_kernel(PassArgs a) {
     using L = OnesweepSmem<B, VB, ITEMS>;
     using VT = typename ValueType<VB>::type;
     constexpr int THREADS = L::THREADS, WARPS = L::WARPS, TILE = L::TILE;
+    static_assert((WARPS * WHIST_WORDS) % 4 == 0 && (WARPS * RANK_MASK_SETS * RADIX) % 4 == 0, "");
     extern __shared__ __align__(16) uint8_t smem[];
     uint32_t *whist = reinterpret_cast<uint32_t *>(smem + L::WHIST);
     uint32_t *wmask = reinterpret_cast<uint32_t *>(smem + L::WMASK);
@@ -248,144 +263,223 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
 
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const B dmask = a.desc ? B(~B(0)) : B(0);
+    const int64_t tiles = int64_t((a.n + TILE - 1) / TILE);
+    const uint32_t seg = warp * 32 * ITEMS;
+    B *kout = static_cast<B *>(a.keys_out);
+    VT *vout = static_cast<VT *>(a.values_out);
+
+    auto zero_scratch = [&]() {
+        uint4 *w4 = reinterpret_cast<uint4 *>(whist);
+        for (uint32_t i = tid; i < WARPS * WHIST_WORDS / 4; i += THREADS) w4[i] = make_uint4(0, 0, 0, 0);
+        uint4 *m4 = reinterpret_cast<uint4 *>(wmask);
+        for (uint32_t i = tid; i < WARPS * RANK_MASK_SETS * RADIX / 4; i += THREADS)
+            m4[i] = make_uint4(0, 0, 0, 0);
+    };
+
+    // Tiles are claimed from the pass's atomic counter.  A tile only ever
+    // waits (look-back) on tiles with smaller ids, and every claimed tile
+    // belongs to a running CTA that has finished all of its own smaller
+    // tiles, so the waits always end.
     if (tid == 0) {
         ctl[0] = atomicAdd(a.tile_counter, 1);
         ctl[1] = 0;
     }
-    for (uint32_t i = tid; i < WARPS * (WHIST_WORDS + RADIX); i += THREADS) whist[i] = 0;  // + wmask
+    zero_scratch();
     __syncthreads();
+    int64_t tile = ctl[0];
+    if (tile >= tiles) return;
 
-    const int64_t tile = ctl[0];
-    const uint64_t base = uint64_t(tile) * TILE;
-    const uint64_t remain = a.n - base;
-    const uint32_t count = remain < uint64_t(TILE) ? uint32_t(remain) : uint32_t(TILE);
-    const bool full = count == uint32_t(TILE);
-    const B *kin = static_cast<const B *>(a.keys_in) + base;
-    const uint32_t seg = warp * 32 * ITEMS;
-
-    // 1. Warp-striped coalesced loads of keys and values; the values are
-    //    fetched now so their DRAM latency overlaps ranking and look-back.
+    // Warp-striped coalesced loads of one tile's keys and values.
+    // (t >= tiles loads nothing; the call is unconditional so the previous
+    // tile's registers are dead after its scatter on every path.)
     B key[ITEMS];
-    if (full) {
-#pragma unroll
-        for (int j = 0; j < ITEMS; ++j) key[j] = ld_stream(kin + seg + j * 32 + lane);
-    } else {
-#pragma unroll
-        for (int j = 0; j < ITEMS; ++j) {
-            const uint32_t pos = seg + j * 32 + lane;
-            key[j] = pos < count ? kin[pos] : B(0);
-        }
-    }
     VT val[VB > 0 ? ITEMS : 1];
-    if constexpr (VB > 0) {
-        const VT *vin = static_cast<const VT *>(a.values_in) + base;
+    auto load_tile = [&](int64_t t) {
+        const uint64_t base = t < tiles ? uint64_t(t) * TILE : 0;
+        const uint64_t remain = t < tiles ? a.n - base : 0;
+        const B *kin = static_cast<const B *>(a.keys_in) + base;
+        if (remain >= uint64_t(TILE)) {
+#pragma unroll
+            for (int j = 0; j < ITEMS; ++j) key[j] = ld_stream(kin + seg + j * 32 + lane);
+        } else {
+#pragma unroll
+            for (int j = 0; j < ITEMS; ++j) {
+                const uint32_t pos = seg + j * 32 + lane;
+                key[j] = pos < remain ? kin[pos] : B(0);
+            }
+        }
+        if constexpr (VB > 0) {
+            const VT *vin = static_cast<const VT *>(a.values_in) + base;
+#pragma unroll
+            for (int j = 0; j < ITEMS; ++j) {
+                const uint32_t pos = seg + j * 32 + lane;
+                if (pos < remain) val[j] = vin[pos];
+            }
+        }
+    };
+    load_tile(tile);
+
+    // One tile: rank, totals and scan, scatter into shared memory, look-back,
+    // write-out.  Returns the next tile id.
+    auto tile_body = [&](auto full_tag, const int64_t tile, const uint32_t count) -> int64_t {
+        constexpr bool FULL = decltype(full_tag)::value;
+        auto live = [&](int j) { return FULL || seg + j * 32 + lane < count; };
+
+        // 1. Stable warp multi-split rank over warp-private histograms.
+        uint32_t rank[ITEMS];
+        if (a.first) {
+#pragma unroll
+            for (int j = 0; j < ITEMS; ++j) key[j] = to_ordered_k<KIND>(key[j], dmask);
+        }
+        auto digit_at = [&](int j) {
+            return live(j) ? digit_k<KIND>(key[j], a.shift, a.mask) : INVALID_DIGIT;
+        };
+#ifdef RSORT_RANK_BALLOT
+        warp_rank_items<ITEMS>(digit_at, rank, whist + warp * RADIX, !FULL);
+#elif RSORT_RANK_MODE == 2
+        warp_rank_items_or3<ITEMS, FULL>(digit_at, rank, whist + warp * WHIST_WORDS,
+                                         wmask + warp * RANK_MASK_SETS * RADIX);
+#else
+        warp_rank_items_or<ITEMS>(digit_at, rank, whist + warp * WHIST_WORDS, wmask + warp * RADIX);
+#endif
+        __syncthreads();
+        const int64_t next = PERSIST ? int64_t(ctl[2]) : tiles;
+
+        // 2. Per-digit tile totals -> look-back aggregate, warp offsets, tile scan.
+        uint32_t total = 0;
+        uint64_t *my_lb = a.lookback + uint64_t(tile) * RADIX + tid;
+#if RSORT_COMBINED_OFFSETS
+        // Each warp's digit counts become absolute tile positions (tile digit
+        // start + the counts of that digit in earlier warps), so the scatter
+        // needs one shared load per key.
+        if (tid < RADIX) {
+#pragma unroll 4
+            for (int w = 0; w < WARPS; ++w) total += whist[w * RADIX + tid];
+            st_relaxed_gpu(my_lb, lb_word(tile == 0 ? LB_INCLUSIVE : LB_AGGREGATE, a.tag, total));
+        }
+        const uint32_t tile_excl = block_exclusive_scan_256(total, wsums, nullptr);
+        if (tid < RADIX) {
+            tstart[tid] = tile_excl;
+            uint32_t run = tile_excl;
+#pragma unroll 4
+            for (int w = 0; w < WARPS; ++w) {
+                const uint32_t t = whist[w * RADIX + tid];
+                whist[w * RADIX + tid] = run;
+                run += t;
+            }
+        }
+#else
+        if (tid < RADIX) {
+#pragma unroll 4
+            for (int w = 0; w < WARPS; ++w) {
+                const uint32_t t = whist[w * RADIX + tid];
+                whist[w * RADIX + tid] = total;
+                total += t;
+            }
+            st_relaxed_gpu(my_lb, lb_word(tile == 0 ? LB_INCLUSIVE : LB_AGGREGATE, a.tag, total));
+        }
+        const uint32_t tile_excl = block_exclusive_scan_256(total, wsums, nullptr);
+        if (tid < RADIX) tstart[tid] = tile_excl;
+#endif
+        __syncthreads();
+
+        // 3. Scatter keys and values into shared memory at their tile rank.
+        bool bad = false;
 #pragma unroll
         for (int j = 0; j < ITEMS; ++j) {
-            const uint32_t pos = seg + j * 32 + lane;
-            if (full || pos < count) val[j] = vin[pos];
+            if (live(j)) {
+#if RSORT_RANK_MODE == 2 && !defined(RSORT_RANK_BALLOT)
+                const uint32_t d = rank[j] >> 16;
+                const uint32_t rj = rank[j] & 0xffffu;
+#else
+                const uint32_t d = digit_k<KIND>(key[j], a.shift, a.mask);
+                const uint32_t rj = rank[j];
+#endif
+#if RSORT_COMBINED_OFFSETS
+                const uint32_t r = whist[warp * RADIX + d] + rj;
+#else
+                const uint32_t r = tstart[d] + whist[warp * RADIX + d] + rj;
+#endif
+                if (r < count) {
+                    skey[r] = key[j];
+                    if constexpr (VB > 0) sval[r] = val[j];
+                } else {
+                    bad = true;
+                }
+            }
         }
-    }
 
-    // 2. Stable warp multi-split rank over warp-private histograms.
-    uint32_t rank[ITEMS];
-    if (a.first) {
-#pragma unroll
-        for (int j = 0; j < ITEMS; ++j) key[j] = to_ordered_k<KIND>(key[j], dmask);
-    }
-    auto digit_at = [&](int j) {
-        return (full || seg + j * 32 + lane < count) ? digit_k<KIND>(key[j], a.shift, a.mask)
-                                                     : INVALID_DIGIT;
+        // 4. Look-back for the exclusive prefix of this tile's digits.
+        if (tid < RADIX) {
+            uint64_t excl = 0;
+            if (tile > 0) {
+                bool gave_up = false;
+                excl = lookback_exclusive(a.lookback, tile, tid, a.tag, a.status, &gave_up);
+                st_relaxed_gpu(my_lb, lb_word(LB_INCLUSIVE, a.tag, excl + total));
+                if (gave_up) ctl[1] = 1;
+            }
+            gbase[tid] = int64_t(a.bins[tid] + excl) - int64_t(tile_excl);
+        }
+        __syncthreads();
+        const bool abort = ctl[1] != 0;
+
+        // 5. The key and value registers are free again: start loading the
+        //    next tile so its DRAM latency overlaps the write-out.
+        if constexpr (PERSIST) load_tile(next);
+
+        // 6. Consecutive threads write consecutive tile positions, i.e. runs
+        //    of consecutive addresses within each digit's output range.
+        auto write_out = [&](auto last_tag) {
+            constexpr bool LAST = decltype(last_tag)::value;
+            auto put = [&](uint32_t i) {
+                const B k = skey[i];
+                const uint32_t d = digit_k<KIND>(k, a.shift, a.mask);
+                const uint64_t dst = uint64_t(gbase[d] + int64_t(i));
+                if (dst < a.n) {
+                    kout[dst] = LAST ? from_ordered_k<KIND>(k, dmask) : k;
+                    if constexpr (VB > 0) vout[dst] = sval[i];
+                } else {
+                    bad = true;
+                }
+            };
+            if constexpr (FULL) {
+                // Fully unrolled unless the next tile's keys are already
+                // loaded (persistent grid), where registers are short.
+                constexpr int WU = PERSIST ? 2 : ITEMS;
+#pragma unroll WU
+                for (int k = 0; k < ITEMS; ++k) put(tid + uint32_t(k) * THREADS);
+            } else {
+                for (uint32_t i = tid; i < count; i += THREADS) put(i);
+            }
+        };
+        if (!abort) {
+            if (a.last)
+                write_out(BoolTag<true>{});
+            else
+                write_out(BoolTag<false>{});
+        }
+        if (bad) atomicExch(a.status, DEV_STATUS_BOUNDS);
+        return next;
     };
-#ifdef RSORT_RANK_BALLOT
-    warp_rank_items<ITEMS>(digit_at, rank, whist + warp * RADIX, !full);
-#else
-    warp_rank_items_or<ITEMS>(digit_at, rank, whist + warp * WHIST_WORDS, wmask + warp * RADIX);
-#endif
-    __syncthreads();
 
-    // 3. Per-digit tile totals -> look-back aggregate, warp offsets, tile scan.
-    uint32_t total = 0;
-    uint64_t *my_lb = a.lookback + uint64_t(tile) * RADIX + tid;
-    if (tid < RADIX) {
-#ifdef RSORT_WHIST16
-        uint16_t *wh16 = reinterpret_cast<uint16_t *>(whist);
-#pragma unroll 4
-        for (int w = 0; w < WARPS; ++w) {
-            const uint32_t t = wh16[w * RADIX + tid];
-            wh16[w * RADIX + tid] = uint16_t(total);
-            total += t;
+    for (;;) {
+        const uint64_t remain = a.n - uint64_t(tile) * TILE;
+        const uint32_t count = remain < uint64_t(TILE) ? uint32_t(remain) : uint32_t(TILE);
+        // Claim the next tile now; it is read after the rank barrier.
+        if constexpr (PERSIST) {
+            if (tid == 0) ctl[2] = atomicAdd(a.tile_counter, 1);
         }
-#else
-#pragma unroll 4
-        for (int w = 0; w < WARPS; ++w) {
-            const uint32_t t = whist[w * RADIX + tid];
-            whist[w * RADIX + tid] = total;
-            total += t;
-        }
-#endif
-        st_relaxed_gpu(my_lb, lb_word(tile == 0 ? LB_INCLUSIVE : LB_AGGREGATE, a.tag, total));
-    }
-    const uint32_t tile_excl = block_exclusive_scan_256(total, wsums, nullptr);
-    if (tid < RADIX) tstart[tid] = tile_excl;
-    __syncthreads();
+        const int64_t next = count == uint32_t(TILE) ? tile_body(BoolTag<true>{}, tile, count)
+                                                     : tile_body(BoolTag<false>{}, tile, count);
+        if (!PERSIST || next >= tiles) break;
 
-    // 4. Scatter keys and values into shared memory at their tile rank (the
-    //    tile rank does not depend on the look-back, so the registers are free
-    //    again before it starts).
-    bool bad = false;
-#pragma unroll
-    for (int j = 0; j < ITEMS; ++j) {
-        const uint32_t pos = seg + j * 32 + lane;
-        if (full || pos < count) {
-            const uint32_t d = digit_k<KIND>(key[j], a.shift, a.mask);
-#ifdef RSORT_WHIST16
-            const uint32_t r = tstart[d] +
-                               reinterpret_cast<const uint16_t *>(whist)[warp * RADIX + d] + rank[j];
-#else
-            const uint32_t r = tstart[d] + whist[warp * RADIX + d] + rank[j];
-#endif
-            if (r < count) {
-                skey[r] = key[j];
-                if constexpr (VB > 0) sval[r] = val[j];
-            } else {
-                bad = true;
-            }
-        }
+        // The staging area aliases the mask arrays: every write-out read is
+        // done before they are cleared for the next tile.
+        __syncthreads();
+        zero_scratch();
+        __syncthreads();
+        tile = next;
     }
-
-    // 5. Look-back for the exclusive prefix of this tile's digits.
-    if (tid < RADIX) {
-        uint64_t excl = 0;
-        if (tile > 0) {
-            bool gave_up = false;
-            excl = lookback_exclusive(a.lookback, tile, tid, a.tag, a.status, &gave_up);
-            st_relaxed_gpu(my_lb, lb_word(LB_INCLUSIVE, a.tag, excl + total));
-            if (gave_up) ctl[1] = 1;
-        }
-        gbase[tid] = int64_t(a.bins[tid] + excl) - int64_t(tile_excl);
-    }
-    __syncthreads();
-    const bool abort = ctl[1] != 0;
-
-    // 6. Consecutive threads write consecutive tile positions, i.e. runs of
-    //    consecutive addresses within each digit's output range.
-    B *kout = static_cast<B *>(a.keys_out);
-    VT *vout = static_cast<VT *>(a.values_out);
-    const int64_t n = int64_t(a.n);
-    if (!abort) {
-        for (uint32_t i = tid; i < count; i += THREADS) {
-            const B k = skey[i];
-            const uint32_t d = digit_k<KIND>(k, a.shift, a.mask);
-            const int64_t dst = gbase[d] + int64_t(i);
-            if (dst >= 0 && dst < n) {
-                kout[dst] = a.last ? from_ordered_k<KIND>(k, dmask) : k;
-                if constexpr (VB > 0) vout[dst] = sval[i];
-            } else {
-                bad = true;
-            }
-        }
-    }
-    if (bad) atomicExch(a.status, DEV_STATUS_BOUNDS);
 }
 
 // ---------------------------------------------------------------------------
@@ -517,12 +611,26 @@ template <typename B, int VB>
 cudaError_t onesweep_t(const PassArgs &a, uint64_t tiles, cudaStream_t s) {
     constexpr int ITEMS = onesweep_items(int(sizeof(B)), VB);
     using L = OnesweepSmem<B, VB, ITEMS>;
-    auto k = a.kind == KIND_FLOAT  ? onesweep_kernel<B, VB, ITEMS, KIND_FLOAT>
-             : a.kind == KIND_SINT ? onesweep_kernel<B, VB, ITEMS, KIND_SINT>
-                                   : onesweep_kernel<B, VB, ITEMS, KIND_UINT>;
+    constexpr bool P = sizeof(B) == 8;
+    auto k = a.kind == KIND_FLOAT  ? onesweep_kernel<B, VB, ITEMS, KIND_FLOAT, P>
+             : a.kind == KIND_SINT ? onesweep_kernel<B, VB, ITEMS, KIND_SINT, P>
+                                   : onesweep_kernel<B, VB, ITEMS, KIND_UINT, P>;
     cudaError_t e = ensure_smem(k, L::BYTES);
     if (e != cudaSuccess) return e;
-    k<<<dim3(uint32_t(tiles)), ONESWEEP_THREADS, L::BYTES, s>>>(a);
+    if (!P) {
+        k<<<dim3(uint32_t(tiles)), ONESWEEP_THREADS, L::BYTES, s>>>(a);
+        return cudaGetLastError();
+    }
+    // Persistent grid: every CTA that fits on the device at once.
+    int dev = 0, sms = 0, per_sm = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, ONESWEEP_THREADS, L::BYTES)) !=
+        cudaSuccess)
+        return e;
+    const uint64_t resident = uint64_t(sms) * uint64_t(per_sm > 0 ? per_sm : 1);
+    const uint64_t grid = tiles < resident ? tiles : resident;
+    k<<<dim3(uint32_t(grid)), ONESWEEP_THREADS, L::BYTES, s>>>(a);
     return cudaGetLastError();
 }
 
