@@ -469,6 +469,13 @@ def run_e2e(args, workload: Workload, keys_h, values_h, dev):
 # N GPUs: distributed sample sort, one process per GPU (weak scaling: every
 # rank holds one workload-sized contiguous shard of the global input)
 # ---------------------------------------------------------------------------
+EXCHANGE_NAMES = {
+    "peer": "first merge round reads the buckets from the peers' shards over NVLink (CUDA IPC)",
+    "peer-copy": "copy kernel pulls the buckets over NVLink (CUDA IPC), then local merge",
+    "nccl": "NCCL grouped send/recv, then local merge",
+}
+
+
 def run_dist(args, workload: Workload):
     import ctypes
     import datetime
@@ -635,15 +642,19 @@ def run_dist(args, workload: Workload):
                         "algorithmic_bytes_per_launch": workload.bytes_per_pass,
                         "avg_launch_ms": avg_s * 1e3}
         phase_ms = dict(zip(ph_names, ph.tolist()))
-        nvlink_gbs = (sent.item() / (phase_ms["exchange"] / 1e3) / 1e9
-                      if phase_ms["exchange"] > 0 else None)
+        # In the default mode the buckets cross NVLink inside the first merge
+        # round, so the bytes are timed over exchange + merge.
+        xfer_ms = phase_ms["exchange"] + (phase_ms["merge"] if os.environ.get(
+            "RSORT_EXCHANGE", "peer") == "peer" else 0.0)
+        nvlink_gbs = sent.item() / (xfer_ms / 1e3) / 1e9 if xfer_ms > 0 else None
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": np.dtype(workload.key).name, "data": "synthetic (numpy PCG64, seeded)",
             "config": dict(config_dict(args, workload), n=world * m, per_gpu_n=m,
-                           parallelism=f"sample sort over {world} GPUs (NCCL all-to-all)"),
+                           parallelism=f"sample sort over {world} GPUs",
+                           exchange=EXCHANGE_NAMES[os.environ.get("RSORT_EXCHANGE", "peer")]),
             "roofline": roofline, "gpu_launches": launches,
             "phases_ms_max_over_ranks": phase_ms,
             "nvlink": {"bytes_per_rank": sent.item(), "achieved_gbs_per_rank": nvlink_gbs,

@@ -193,6 +193,47 @@ rsort_status rsort_merge_runs(rsort_key_t key, int descending, void *keys, void 
                               void *scratch_keys, void *scratch_values, uint64_t *d_partitions,
                               size_t npartitions, int *result_in_scratch, rsort_stream_t stream);
 
+/* Stable merge of `runs` sorted runs that may live anywhere the device can
+ * read -- this GPU's memory or a peer's (IPC-mapped): the first round merges
+ * runs (0,1), (2,3), ... straight from the given pointers into out, so a
+ * peer's run crosses NVLink once, inside the merge; later rounds go between
+ * out and scratch.  Host arrays of run pointers and lengths; ties keep the
+ * lower run first.  The result is in out, or in scratch when
+ * *result_in_scratch is set.  d_partitions as for rsort_merge_runs. */
+rsort_status rsort_merge_segments(rsort_key_t key, int descending, unsigned runs,
+                                  const void *const *run_keys, const void *const *run_values,
+                                  const size_t *run_lengths, size_t value_bytes, void *out_keys,
+                                  void *out_values, void *scratch_keys, void *scratch_values,
+                                  uint64_t *d_partitions, size_t npartitions,
+                                  int *result_in_scratch, rsort_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Bucket exchange over NVLink peer memory (no reference counterpart).
+ *
+ * Replaces step 5 above (the NCCL all-to-all): every rank exports its sorted
+ * shard with CUDA IPC, maps the peers' shards once, and either merges its
+ * buckets straight out of the peers' shards (rsort_merge_segments) or pulls
+ * them with one copy kernel reading peer HBM directly.
+ *   rsort_ipc_export   IPC handle (RSORT_IPC_HANDLE_BYTES) of the device
+ *                      allocation holding d_ptr, and d_ptr's byte offset in it
+ *   rsort_ipc_import   maps a peer's handle (same node); d_base + offset is
+ *                      the peer's pointer; undo with rsort_ipc_release
+ *   rsort_gather_segments  copies nseg device segments (peer or local, host
+ *                      arrays of pointers and byte lengths) back to back into
+ *                      d_dst on `stream`; nseg <= RSORT_GATHER_MAX_SEGMENTS
+ * The kernel does not wait for the peers: order it after every peer's sort
+ * (for example a collective entered after the sort) and order the peers'
+ * next writes of their shards after it (a collective after the copy).
+ * ------------------------------------------------------------------------- */
+#define RSORT_IPC_HANDLE_BYTES 64
+#define RSORT_GATHER_MAX_SEGMENTS 64
+
+rsort_status rsort_ipc_export(const void *d_ptr, void *handle, uint64_t *offset);
+rsort_status rsort_ipc_import(const void *handle, void **d_base);
+rsort_status rsort_ipc_release(void *d_base);
+rsort_status rsort_gather_segments(unsigned nseg, const void *const *d_src, const uint64_t *bytes,
+                                   void *d_dst, rsort_stream_t stream);
+
 /* ---------------------------------------------------------------------------
  * Allocation-free keys sort (no reference counterpart).
  *
@@ -228,7 +269,8 @@ void rsort_launch_count_reset(void);
 
 /* Kernel ids reported by rsort_profile_read. */
 enum { RSORT_KERNEL_INIT = 0, RSORT_KERNEL_HISTOGRAM = 1, RSORT_KERNEL_ONESWEEP = 2,
-       RSORT_KERNEL_SINGLE_TILE = 3, RSORT_KERNEL_DIST = 4, RSORT_KERNEL_MERGE = 5 };
+       RSORT_KERNEL_SINGLE_TILE = 3, RSORT_KERNEL_DIST = 4, RSORT_KERNEL_MERGE = 5,
+       RSORT_KERNEL_GATHER = 6 };
 
 /* Benchmark instrumentation (no reference counterpart): while enabled, every
  * kernel launch of the calling host thread is bracketed by CUDA events on its

@@ -28,7 +28,9 @@ RSORT_BAD_ARGUMENT = 8
 
 # kernel ids of rsort_profile_read
 KERNEL_NAMES = {0: "init", 1: "histogram", 2: "onesweep", 3: "single_tile", 4: "dist",
-                5: "merge"}
+                5: "merge", 6: "gather"}
+IPC_HANDLE_BYTES = 64
+GATHER_MAX_SEGMENTS = 64
 
 EXPORTED_SYMBOLS = (
     "rsort_controls_query",
@@ -53,6 +55,11 @@ EXPORTED_SYMBOLS = (
     "rsort_merge_runs",
     "rsort_keys_static",
     "rsort_selftest_lookback_timeout",
+    "rsort_ipc_export",
+    "rsort_ipc_import",
+    "rsort_ipc_release",
+    "rsort_gather_segments",
+    "rsort_merge_segments",
 )
 
 
@@ -121,6 +128,18 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.rsort_keys_static.restype = i
     lib.rsort_selftest_lookback_timeout.argtypes = [vp]
     lib.rsort_selftest_lookback_timeout.restype = i
+    lib.rsort_ipc_export.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_uint64)]
+    lib.rsort_ipc_export.restype = i
+    lib.rsort_ipc_import.argtypes = [vp, ctypes.POINTER(vp)]
+    lib.rsort_ipc_import.restype = i
+    lib.rsort_ipc_release.argtypes = [vp]
+    lib.rsort_ipc_release.restype = i
+    lib.rsort_gather_segments.argtypes = [u, ctypes.POINTER(vp), ctypes.POINTER(ctypes.c_uint64),
+                                          vp, vp]
+    lib.rsort_gather_segments.restype = i
+    lib.rsort_merge_segments.argtypes = [i, i, u, ctypes.POINTER(vp), ctypes.POINTER(vp),
+                                         ctypes.POINTER(sz), sz, vp, vp, vp, vp, vp, sz, pi, vp]
+    lib.rsort_merge_segments.restype = i
 
 
 def lib() -> ctypes.CDLL:

@@ -497,6 +497,70 @@ rsort_status rsort_dist_bounds(rsort_key_t key, int descending, const void *d_so
     return e == cudaSuccess ? RSORT_OK : cuda_fail(e, "bounds launch");
 }
 
+rsort_status rsort_ipc_export(const void *d_ptr, void *handle, uint64_t *offset) {
+    if (!d_ptr || !handle || !offset) return fail(RSORT_BAD_ARGUMENT, "null argument");
+    uintptr_t base = 0;
+    cudaError_t e = allocation_base(d_ptr, &base);
+    if (e != cudaSuccess) return cuda_fail(e, "allocation base of the exported pointer");
+    cudaIpcMemHandle_t h;
+    e = cudaIpcGetMemHandle(&h, reinterpret_cast<void *>(base));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+    static_assert(sizeof(h) == RSORT_IPC_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(handle, &h, sizeof(h));
+    *offset = uint64_t(reinterpret_cast<uintptr_t>(d_ptr) - base);
+    return RSORT_OK;
+}
+
+rsort_status rsort_ipc_import(const void *handle, void **d_base) {
+    if (!handle || !d_base) return fail(RSORT_BAD_ARGUMENT, "null argument");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    const cudaError_t e = cudaIpcOpenMemHandle(d_base, h, cudaIpcMemLazyEnablePeerAccess);
+    return e == cudaSuccess ? RSORT_OK : cuda_fail(e, "cudaIpcOpenMemHandle");
+}
+
+rsort_status rsort_ipc_release(void *d_base) {
+    if (!d_base) return fail(RSORT_BAD_ARGUMENT, "null argument");
+    const cudaError_t e = cudaIpcCloseMemHandle(d_base);
+    return e == cudaSuccess ? RSORT_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+rsort_status rsort_gather_segments(unsigned nseg, const void *const *d_src, const uint64_t *bytes,
+                                   void *d_dst, rsort_stream_t stream) {
+    if (nseg > unsigned(GATHER_MAX_SEGMENTS))
+        return fail(RSORT_BAD_ARGUMENT, "gather segment count", GATHER_MAX_SEGMENTS, nseg);
+    if (nseg == 0) return RSORT_OK;
+    if (!d_src || !bytes) return fail(RSORT_BAD_ARGUMENT, "null argument");
+    GatherArgs a{};
+    a.nseg = nseg;
+    a.dst = static_cast<char *>(d_dst);
+    uint64_t total = 0;
+    for (unsigned q = 0; q < nseg; ++q) {
+        a.dst_start[q] = total;
+        a.src[q] = static_cast<const char *>(d_src[q]);
+        if (bytes[q] && !d_src[q]) return fail(RSORT_BAD_ARGUMENT, "null segment");
+        const uint64_t align = uint64_t(reinterpret_cast<uintptr_t>(d_src[q])) |
+                               uint64_t(reinterpret_cast<uintptr_t>(a.dst) + total) | bytes[q];
+        int lg = 0;
+        while (lg < 4 && !(align & (uint64_t(1) << lg))) ++lg;
+        a.unit_log2[q] = uint8_t(lg);
+        total += bytes[q];
+    }
+    a.dst_start[nseg] = total;
+    if (total == 0) return RSORT_OK;
+    if (!d_dst) return fail(RSORT_BAD_ARGUMENT, "null buffer");
+    DeviceInfo dev;
+    rsort_status st = device_info(&dev);
+    if (st != RSORT_OK) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    {
+        LaunchScope scope(RSORT_KERNEL_GATHER, s);
+        e = launch_gather(a, dev.sm_count, s);
+    }
+    return e == cudaSuccess ? RSORT_OK : cuda_fail(e, "gather launch");
+}
+
 size_t rsort_merge_partition_words(size_t total) { return merge_partition_words(total, 0); }
 
 rsort_status rsort_merge(rsort_key_t key, int descending, const void *a_keys,
@@ -581,6 +645,55 @@ rsort_status rsort_merge_runs(rsort_key_t key, int descending, void *keys, void 
     }
     *result_in_scratch = in_scratch ? 1 : 0;
     return RSORT_OK;
+}
+
+
+rsort_status rsort_merge_segments(rsort_key_t key, int descending, unsigned runs,
+                                  const void *const *run_keys, const void *const *run_values,
+                                  const size_t *run_lengths, size_t value_bytes, void *out_keys,
+                                  void *out_values, void *scratch_keys, void *scratch_values,
+                                  uint64_t *d_partitions, size_t npartitions,
+                                  int *result_in_scratch, rsort_stream_t stream) {
+    if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
+    if (!value_ok(value_bytes)) return fail(RSORT_BAD_ARGUMENT, "radix value width");
+    if (!result_in_scratch || (runs && (!run_lengths || !run_keys || (value_bytes && !run_values))))
+        return fail(RSORT_BAD_ARGUMENT, "null argument");
+    *result_in_scratch = 0;
+    const size_t kb = size_t(key_bytes(key));
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    char *ok = static_cast<char *>(out_keys), *ov = static_cast<char *>(out_values);
+    // First round straight from the given runs (a peer's memory is read once,
+    // by the merge itself): pairs (0,1), (2,3), ... into out.
+    std::vector<size_t> len;
+    size_t off = 0;
+    for (unsigned r = 0; r < runs; r += 2) {
+        if (r + 1 < runs) {
+            rsort_status st = rsort_merge(key, descending, run_keys[r],
+                                          value_bytes ? run_values[r] : nullptr, run_lengths[r],
+                                          run_keys[r + 1], value_bytes ? run_values[r + 1] : nullptr,
+                                          run_lengths[r + 1], ok + off * kb,
+                                          value_bytes ? ov + off * value_bytes : nullptr,
+                                          value_bytes, d_partitions, npartitions, stream);
+            if (st != RSORT_OK) return st;
+            len.push_back(run_lengths[r] + run_lengths[r + 1]);
+        } else {
+            if (run_lengths[r]) {
+                cudaError_t e = cudaMemcpyAsync(ok + off * kb, run_keys[r], run_lengths[r] * kb,
+                                                cudaMemcpyDeviceToDevice, s);
+                if (e == cudaSuccess && value_bytes)
+                    e = cudaMemcpyAsync(ov + off * value_bytes, run_values[r],
+                                        run_lengths[r] * value_bytes, cudaMemcpyDeviceToDevice, s);
+                if (e != cudaSuccess) return cuda_fail(e, "merge run copy");
+            }
+            len.push_back(run_lengths[r]);
+        }
+        off += len.back();
+    }
+    if (len.size() <= 1) return RSORT_OK;
+    // Later rounds in local memory, between out and scratch.
+    return rsort_merge_runs(key, descending, out_keys, out_values, value_bytes, len.data(),
+                            unsigned(len.size()), scratch_keys, scratch_values, d_partitions,
+                            npartitions, result_in_scratch, stream);
 }
 
 // Failure-detection self test: one onesweep CTA is handed tile 1 of a

@@ -115,7 +115,12 @@ __global__ void bounds_kernel(const B *keys, uint64_t m, uint32_t rank, const Co
 // merges MERGE_ITEMS outputs per thread and writes the tile out coalesced.
 // ---------------------------------------------------------------------------
 constexpr int MERGE_THREADS = 256;
-constexpr int MERGE_ITEMS = 16;
+// Odd, so the serial per-thread merges of neighbouring lanes (which start
+// MERGE_ITEMS items apart in shared memory) fall into different banks.
+#ifndef RSORT_MERGE_ITEMS
+#define RSORT_MERGE_ITEMS 11
+#endif
+constexpr int MERGE_ITEMS = RSORT_MERGE_ITEMS;
 constexpr int MERGE_TILE = MERGE_THREADS * MERGE_ITEMS;
 
 template <typename B>
@@ -184,13 +189,28 @@ __global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(MergeArgs p, const
     const uint64_t b0 = d0 - a0, b1 = d1 - a1;
     const uint32_t la = uint32_t(a1 - a0), lb = uint32_t(b1 - b0);
     const uint32_t n = la + lb;
-    for (uint32_t i = threadIdx.x; i < n; i += MERGE_THREADS) {
-        if (i < la) {
-            sk[i] = ak[a0 + i];
-            if constexpr (VB > 0) sv[i] = av[a0 + i];
-        } else {
-            sk[i] = bk[b0 + i - la];
-            if constexpr (VB > 0) sv[i] = bv[b0 + i - la];
+    {
+        // Every load of the thread is issued before the first shared store,
+        // so MERGE_ITEMS keys (and values) per thread are in flight at once:
+        // the runs may be a peer's memory, microseconds away over NVLink.
+        B kreg[MERGE_ITEMS];
+        VT vreg[VB > 0 ? MERGE_ITEMS : 1];
+#pragma unroll
+        for (int k = 0; k < MERGE_ITEMS; ++k) {
+            const uint32_t i = threadIdx.x + uint32_t(k) * MERGE_THREADS;
+            if (i < n) {
+                const bool in_a = i < la;
+                kreg[k] = in_a ? ak[a0 + i] : bk[b0 + i - la];
+                if constexpr (VB > 0) vreg[k] = in_a ? av[a0 + i] : bv[b0 + i - la];
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < MERGE_ITEMS; ++k) {
+            const uint32_t i = threadIdx.x + uint32_t(k) * MERGE_THREADS;
+            if (i < n) {
+                sk[i] = kreg[k];
+                if constexpr (VB > 0) sv[i] = vreg[k];
+            }
         }
     }
     __syncthreads();

@@ -44,4 +44,19 @@ size_t merge_partition_words(uint64_t na, uint64_t nb);
 cudaError_t launch_merge(int key_bytes, int value_bytes, const MergeArgs &p, uint64_t *split,
                          cudaStream_t s);
 
+// Segment gather of the bucket exchange: segment q (src[q], a peer's or the
+// local shard) lands at dst + dst_start[q]; unit_log2[q] is the copy width
+// (log2 bytes, at most 4) that divides both addresses and the length.
+constexpr int GATHER_MAX_SEGMENTS = 64;
+struct GatherArgs {
+    const char *src[GATHER_MAX_SEGMENTS];
+    uint64_t dst_start[GATHER_MAX_SEGMENTS + 1];
+    uint8_t unit_log2[GATHER_MAX_SEGMENTS];
+    char *dst;
+    uint32_t nseg;
+};
+cudaError_t launch_gather(const GatherArgs &a, int sm_count, cudaStream_t s);
+// Base address of the device allocation that contains p.
+cudaError_t allocation_base(const void *p, uintptr_t *base);
+
 }  // namespace rsort

@@ -8,8 +8,10 @@ One process per GPU.  Rank r holds a contiguous shard of the global input.
   3. all-gather of the samples over NCCL
   4. W-1 splitters from the sorted sample set (device kernel)
   5. bucket bounds of every splitter in the local shard (device kernel)
-  6. all-to-all of the bucket sizes, then of the key and value buckets
-     (NCCL grouped send/recv inside torch.distributed.all_to_all_single)
+  6. all-gather of every rank's bucket sizes and shard IPC handles, then
+     each rank pulls its bucket out of every peer's shard with one copy
+     kernel over NVLink peer memory (PeerExchange); NCCL grouped send/recv
+     is the fallback when the shards cannot be exported
   7. stable merge of the W received runs (device merge-path kernel)
 The composite order is the global stable order, so the ranks' outputs,
 concatenated in rank order, are the stable sort of the concatenated input.
@@ -19,7 +21,11 @@ drive W simulated ranks through exactly the same steps.
 """
 from __future__ import annotations
 
+import atexit
 import ctypes
+import os
+import threading
+from collections import OrderedDict
 from typing import List, Optional, Sequence, Tuple
 
 import torch
@@ -141,16 +147,26 @@ def _bytes(t: torch.Tensor) -> torch.Tensor:
 
 def sample_sort(keys: torch.Tensor, values: Optional[torch.Tensor] = None,
                 descending: bool = False, group=None, samples_per_rank: Optional[int] = None,
-                ops=None, timings: Optional[dict] = None):
+                ops=None, timings: Optional[dict] = None, exchange_mode: Optional[str] = None):
     """Globally sort the ranks' shards; returns this rank's (keys, values) part.
 
     Sorts `keys` / `values` in place as its first step.  The output partition
-    sizes are data dependent."""
+    sizes are data dependent.  exchange_mode (default: the RSORT_EXCHANGE
+    environment variable, else "peer"):
+      "peer"       the first merge round reads the buckets straight out of the
+                   peers' shards over NVLink (CUDA IPC); no staging copy
+      "peer-copy"  one copy kernel pulls the buckets over NVLink, then the
+                   local merge
+      "nccl"       NCCL grouped send/recv, then the local merge"""
     import torch.distributed as dist
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     if ops is None:
         ops = CudaLocalOps(Program.load(keys.device).on())
+    mode = exchange_mode or os.environ.get("RSORT_EXCHANGE", "peer")
+    if mode not in ("peer", "peer-copy", "nccl"):
+        raise ValueError(f"exchange mode {mode!r}: expected 'peer', 'peer-copy' or 'nccl'")
+    peer = mode in ("peer", "peer-copy") and keys.is_cuda and world > 1
     S = samples_per_rank or default_samples_per_rank(world)
     ev = _Events(timings, keys.device)
     ev.mark("start")
@@ -160,21 +176,178 @@ def sample_sort(keys: torch.Tensor, values: Optional[torch.Tensor] = None,
     dist.all_gather(gathered, samples, group=group)
     gathered = torch.cat(gathered)
     send = phase_partition(ops, keys, gathered, rank, world, descending)
-    recv = torch.empty_like(send)
-    dist.all_to_all_single(recv, send, group=group)
-    send_l, recv_l = send.tolist(), recv.tolist()
+    if peer:
+        # One all-gather carries every rank's bucket sizes and shard handles;
+        # it also orders the peer reads after every rank's sort.
+        px = peer_exchange()
+        rec = torch.cat([send, px.record(keys, values, send.device)])
+        table = [torch.empty_like(rec) for _ in range(world)]
+        dist.all_gather(table, rec, group=group)
+        table = torch.stack(table).cpu()
+        sizes = table[:, :world].tolist()
+        peer = bool(table[:, world].all())
+        recv_l = [sizes[q][rank] for q in range(world)]
+    else:
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=group)
+        send_l, recv_l = send.tolist(), recv.tolist()
     ev.mark("partition")
+    if peer and mode == "peer":
+        # No separate exchange: the first merge round reads the buckets
+        # straight out of the peers' shards.
+        ev.mark("exchange")
+        out = px.merge(keys, values, table, sizes, rank, world, ops.launch.handle, descending)
+        # The peers may overwrite their shards only after every rank's merge.
+        dist.all_reduce(torch.zeros(1, device=keys.device), group=group)
+        ev.mark("merge")
+        ev.finish()
+        return out
     out_k = torch.empty(sum(recv_l), dtype=keys.dtype, device=keys.device)
     out_v = None
     if values is not None:
         shape = (sum(recv_l),) + tuple(values.shape[1:])
         out_v = torch.empty(shape, dtype=values.dtype, device=values.device)
-    exchange(keys, values, out_k, out_v, send_l, recv_l, rank, world, group)
+    if peer:
+        px.pull(keys, values, out_k, out_v, table, sizes, rank, world, ops.launch.handle)
+        # The peers may overwrite their shards only after every rank's pull.
+        dist.all_reduce(torch.zeros(1, device=keys.device), group=group)
+    else:
+        if mode in ("peer", "peer-copy") and keys.is_cuda and world > 1:
+            send_l = [sizes[rank][q] for q in range(world)]
+        exchange(keys, values, out_k, out_v, send_l, recv_l, rank, world, group)
     ev.mark("exchange")
     out = phase_merge(ops, out_k, out_v, recv_l, descending)
     ev.mark("merge")
     ev.finish()
     return out
+
+
+class PeerExchange:
+    """Bucket exchange by direct reads of the peers' shards over NVLink.
+
+    Each rank exports its sorted shard (keys, values) as CUDA IPC handles; a
+    peer maps a handle once (kept in a small cache, released at exit) and
+    pulls its bucket with rsort_gather_segments, one SM-driven copy kernel
+    that reads every peer at once.  A shard that cannot be exported (for
+    example memory from a VMM-based allocator) makes every rank fall back to
+    the NCCL exchange, since all ranks see the same export flags."""
+
+    WORDS = 1 + 2 * (_lib.IPC_HANDLE_BYTES // 8 + 1)  # flag, (handle, offset) x 2
+    CACHE = 64
+
+    def __init__(self):
+        self._mapped: "OrderedDict[bytes, int]" = OrderedDict()
+        self._lock = threading.Lock()
+
+    def _export(self, t: Optional[torch.Tensor]) -> Tuple[bytes, int, bool]:
+        if t is None or t.numel() == 0:
+            return bytes(_lib.IPC_HANDLE_BYTES), 0, True
+        h = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+        off = ctypes.c_uint64(0)
+        st = _lib.lib().rsort_ipc_export(t.data_ptr(), h, ctypes.byref(off))
+        return h.raw, off.value, st == 0
+
+    def record(self, keys, values, device) -> torch.Tensor:
+        """flag, key handle + offset, value handle + offset as int64 words."""
+        kh, ko, kok = self._export(keys)
+        vh, vo, vok = self._export(values)
+        words = [1 if (kok and vok) else 0]
+        for h, o in ((kh, ko), (vh, vo)):
+            words += list(memoryview(h).cast("q"))
+            words.append(o)
+        return torch.tensor(words, dtype=torch.int64).to(device)
+
+    def _base(self, handle: bytes) -> int:
+        with self._lock:
+            if handle in self._mapped:
+                self._mapped.move_to_end(handle)
+                return self._mapped[handle]
+            p = ctypes.c_void_p(0)
+            raise_for(_lib.lib().rsort_ipc_import(handle, ctypes.byref(p)))
+            self._mapped[handle] = p.value
+            while len(self._mapped) > self.CACHE:
+                _, old = self._mapped.popitem(last=False)
+                _lib.lib().rsort_ipc_release(ctypes.c_void_p(old))
+            return p.value
+
+    def pull(self, keys, values, out_k, out_v, table, sizes, rank: int, world: int, stream) -> None:
+        hw = _lib.IPC_HANDLE_BYTES // 8
+        kb = keys.element_size()
+        vb = value_bytes_of(values) if values is not None else 0
+        for which, local, out, width in ((0, keys, out_k, kb), (1, values, out_v, vb)):
+            if width == 0:
+                continue
+            col = world + 1 + which * (hw + 1)
+            srcs = (ctypes.c_void_p * world)()
+            lens = (ctypes.c_uint64 * world)()
+            for q in range(world):
+                start = sum(sizes[q][:rank])
+                lens[q] = sizes[q][rank] * width
+                if lens[q] == 0:
+                    srcs[q] = None
+                elif q == rank:
+                    srcs[q] = local.data_ptr() + start * width
+                else:
+                    handle = table[q, col:col + hw].numpy().tobytes()
+                    off = int(table[q, col + hw])
+                    srcs[q] = self._base(handle) + off + start * width
+            raise_for(_lib.lib().rsort_gather_segments(world, srcs, lens, out.data_ptr(), stream))
+
+    def merge(self, keys, values, table, sizes, rank: int, world: int, stream, descending):
+        """Merge this rank's W buckets straight out of the shards (peers' over
+        NVLink, the local one from HBM) into new tensors."""
+        hw = _lib.IPC_HANDLE_BYTES // 8
+        kb = keys.element_size()
+        vb = value_bytes_of(values) if values is not None else 0
+        n_out = sum(sizes[q][rank] for q in range(world))
+        kp = (ctypes.c_void_p * world)()
+        vp = (ctypes.c_void_p * world)()
+        lens = (ctypes.c_size_t * world)()
+        for q in range(world):
+            start = sum(sizes[q][:rank])
+            lens[q] = sizes[q][rank]
+            for which, local, width, arr in ((0, keys, kb, kp), (1, values, vb, vp)):
+                if width == 0 or lens[q] == 0:
+                    continue
+                if q == rank:
+                    arr[q] = local.data_ptr() + start * width
+                else:
+                    col = world + 1 + which * (hw + 1)
+                    handle = table[q, col:col + hw].numpy().tobytes()
+                    arr[q] = self._base(handle) + int(table[q, col + hw]) + start * width
+        out_k = torch.empty(n_out, dtype=keys.dtype, device=keys.device)
+        sk = torch.empty_like(out_k)
+        out_v = sv = None
+        if values is not None:
+            shape = (n_out,) + tuple(values.shape[1:])
+            out_v = torch.empty(shape, dtype=values.dtype, device=values.device)
+            sv = torch.empty_like(out_v)
+        nparts = _lib.lib().rsort_merge_partition_words(n_out)
+        parts = torch.empty(max(nparts, 1), dtype=torch.int64, device=keys.device)
+        in_scratch = ctypes.c_int(0)
+        raise_for(_lib.lib().rsort_merge_segments(
+            key_code(keys.dtype), int(descending), world, kp, vp, lens, vb, out_k.data_ptr(),
+            None if out_v is None else out_v.data_ptr(), sk.data_ptr(),
+            None if sv is None else sv.data_ptr(), parts.data_ptr(), nparts,
+            ctypes.byref(in_scratch), stream))
+        return (sk, sv) if in_scratch.value else (out_k, out_v)
+
+    def close(self) -> None:
+        with self._lock:
+            while self._mapped:
+                _, p = self._mapped.popitem()
+                _lib.lib().rsort_ipc_release(ctypes.c_void_p(p))
+
+
+_PEER: Optional[PeerExchange] = None
+
+
+def peer_exchange() -> PeerExchange:
+    global _PEER
+    if _PEER is None:
+        _PEER = PeerExchange()
+        atexit.register(_PEER.close)
+    return _PEER
 
 
 def exchange(keys, values, out_k, out_v, send_l, recv_l, rank: int, world: int, group=None):
