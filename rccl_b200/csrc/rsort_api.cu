@@ -717,7 +717,12 @@ rsort_status rsort_selftest_lookback_timeout(rsort_stream_t stream) {
     if (e == cudaSuccess) e = cudaMalloc(&counters, CTR_WORDS * 4);
     if (e == cudaSuccess) e = cudaMemsetAsync(keys, 0, n * 4, s);
     if (e == cudaSuccess) e = cudaMemsetAsync(out, 0, n * 4, s);
-    if (e == cudaSuccess) e = cudaMemsetAsync(bins, 0, RADIX * 8, s);
+    // Two non-empty digit buckets (digit 0 and digit 255, n/2 keys each), so
+    // the pass is not a one-bucket identity copy and the tile must look back.
+    std::vector<uint64_t> host_bins(RADIX, n / 2);
+    host_bins[0] = 0;
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(bins, host_bins.data(), RADIX * 8, cudaMemcpyHostToDevice, s);
     if (e == cudaSuccess) e = cudaMemsetAsync(lookback, 0, 2 * RADIX * 8, s);
     if (e == cudaSuccess) e = cudaMemsetAsync(counters, 0, CTR_WORDS * 4, s);
     const int32_t one = 1;  // the single CTA claims tile 1

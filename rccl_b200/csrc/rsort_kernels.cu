@@ -283,6 +283,7 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
     if (tid == 0) {
         ctl[0] = atomicAdd(a.tile_counter, 1);
         ctl[1] = 0;
+        ctl[3] = 0;
     }
     zero_scratch();
     __syncthreads();
@@ -318,6 +319,47 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
         }
     };
     load_tile(tile);
+
+    // One-bucket fast path: when one digit holds all n keys the pass is the
+    // identity permutation, so every tile is copied through in place (with
+    // the first / last pass transforms) at HBM speed.  The bins are the same
+    // for every CTA, so all CTAs take the same path and no tile waits on
+    // another.  The pass still writes the alternate buffer, so the selector
+    // outcome is unchanged.
+    if (tid < RADIX) {
+        const uint64_t lo = a.bins[tid];
+        const uint64_t hi = tid + 1 < RADIX ? a.bins[tid + 1] : a.n;
+        if (hi - lo == a.n) ctl[3] = 1;
+    }
+    __syncthreads();
+    if (ctl[3]) {
+        for (;;) {
+            const uint64_t base = uint64_t(tile) * TILE;
+            const uint64_t remain = a.n - base;
+            if constexpr (PERSIST) {
+                if (tid == 0) ctl[2] = atomicAdd(a.tile_counter, 1);
+            }
+#pragma unroll
+            for (int j = 0; j < ITEMS; ++j) {
+                const uint32_t pos = seg + j * 32 + lane;
+                if (pos < remain) {
+                    B k = key[j];
+                    if (a.first) k = to_ordered_k<KIND>(k, dmask);
+                    if (a.last) k = from_ordered_k<KIND>(k, dmask);
+                    kout[base + pos] = k;
+                    if constexpr (VB > 0) vout[base + pos] = val[j];
+                }
+            }
+            if constexpr (!PERSIST) break;
+            __syncthreads();
+            const int64_t next = ctl[2];
+            __syncthreads();  // the next claim rewrites ctl[2]
+            if (next >= tiles) break;
+            tile = next;
+            load_tile(tile);
+        }
+        return;
+    }
 
     // One tile: rank, totals and scan, scatter into shared memory, look-back,
     // write-out.  Returns the next tile id.

@@ -176,6 +176,29 @@ def test_keys_skewed_parity(launch, kname, mode):
         check_against_oracle(launch, gen_keys(rng, NP_OF[kname], 70_001, mode), None, desc)
 
 
+@pytest.mark.parametrize("kname", KEY_NAMES)
+@pytest.mark.parametrize("with_values", [False, True])
+def test_one_bucket_passes(launch, kname, with_values):
+    """Keys whose high digits are the same for every key: those passes take
+    the one-bucket identity path (a transformed copy), the others sort."""
+    rng = np.random.default_rng(17)
+    dt = NP_OF[kname]
+    n = 100_003
+    if dt in (np.float32, np.float64):
+        k = rng.uniform(1.0, 1.5, n).astype(dt)  # one sign, one exponent
+    elif np.issubdtype(dt, np.signedinteger):
+        k = rng.integers(0, 3000, n).astype(dt)  # non-negative: top digits constant
+    else:
+        k = rng.integers(0, 3000, n).astype(dt)
+    k[::101] = k[5]  # duplicates: stability through identity passes
+    v = np.arange(n, dtype=np.uint32) if with_values else None
+    for desc in (False, True):
+        check_against_oracle(launch, k, v, desc)
+        # a partial window whose every pass is a single bucket
+        width = np.dtype(dt).itemsize * 8
+        check_against_oracle(launch, k, v, desc, (width - 4, width))
+
+
 @pytest.mark.parametrize("kname", ["uint32", "float32", "uint64", "int64"])
 @pytest.mark.parametrize("vb", [1, 2, 4, 8, 16])
 @pytest.mark.parametrize("n", [777, 2305, 4865, 50_001])
