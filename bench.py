@@ -160,15 +160,23 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.lines = []
+        self._first = threading.Event()
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.reader = threading.Thread(target=self._read, daemon=True)
             self.reader.start()
+            # nvidia-smi takes a moment to start: wait for its first sample so
+            # the timed region (often ~0.1 s) is covered from its start; only
+            # samples taken after that point are kept.
+            t0 = time.time()
+            while not self._first.wait(0.05) and time.time() - t0 < 5:
+                pass
+            self.lines.clear()
         except OSError:
             self.proc = None
         return self
@@ -176,6 +184,7 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
+            self._first.set()
 
     def __exit__(self, *exc):
         if self.proc:

@@ -199,13 +199,17 @@ rsort_status rsort_merge_runs(rsort_key_t key, int descending, void *keys, void 
  * peer's run crosses NVLink once, inside the merge; later rounds go between
  * out and scratch.  Host arrays of run pointers and lengths; ties keep the
  * lower run first.  The result is in out, or in scratch when
- * *result_in_scratch is set.  d_partitions as for rsort_merge_runs. */
+ * *result_in_scratch is set.  d_partitions as for rsort_merge_runs.
+ * first_pair: the first-round pair launched first (the others follow,
+ * wrapping); ranks starting at different pairs spread their peer reads over
+ * different peers.  It does not change the result. */
 rsort_status rsort_merge_segments(rsort_key_t key, int descending, unsigned runs,
                                   const void *const *run_keys, const void *const *run_values,
                                   const size_t *run_lengths, size_t value_bytes, void *out_keys,
                                   void *out_values, void *scratch_keys, void *scratch_values,
                                   uint64_t *d_partitions, size_t npartitions,
-                                  int *result_in_scratch, rsort_stream_t stream);
+                                  int *result_in_scratch, unsigned first_pair,
+                                  rsort_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * Bucket exchange over NVLink peer memory (no reference counterpart).

@@ -138,7 +138,8 @@ def _declare(lib: ctypes.CDLL) -> None:
                                           vp, vp]
     lib.rsort_gather_segments.restype = i
     lib.rsort_merge_segments.argtypes = [i, i, u, ctypes.POINTER(vp), ctypes.POINTER(vp),
-                                         ctypes.POINTER(sz), sz, vp, vp, vp, vp, vp, sz, pi, vp]
+                                         ctypes.POINTER(sz), sz, vp, vp, vp, vp, vp, sz, pi, u,
+                                         vp]
     lib.rsort_merge_segments.restype = i
 
 

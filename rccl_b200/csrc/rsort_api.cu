@@ -653,7 +653,8 @@ rsort_status rsort_merge_segments(rsort_key_t key, int descending, unsigned runs
                                   const size_t *run_lengths, size_t value_bytes, void *out_keys,
                                   void *out_values, void *scratch_keys, void *scratch_values,
                                   uint64_t *d_partitions, size_t npartitions,
-                                  int *result_in_scratch, rsort_stream_t stream) {
+                                  int *result_in_scratch, unsigned first_pair,
+                                  rsort_stream_t stream) {
     if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
     if (!value_ok(value_bytes)) return fail(RSORT_BAD_ARGUMENT, "radix value width");
     if (!result_in_scratch || (runs && (!run_lengths || !run_keys || (value_bytes && !run_values))))
@@ -663,10 +664,23 @@ rsort_status rsort_merge_segments(rsort_key_t key, int descending, unsigned runs
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     char *ok = static_cast<char *>(out_keys), *ov = static_cast<char *>(out_values);
     // First round straight from the given runs (a peer's memory is read once,
-    // by the merge itself): pairs (0,1), (2,3), ... into out.
-    std::vector<size_t> len;
+    // by the merge itself): pairs (0,1), (2,3), ... into out, launched from
+    // pair first_pair on (wrapping), so ranks that start at different pairs
+    // read different peers at the same time.  The output layout does not
+    // depend on the launch order.
+    const unsigned pairs = (runs + 1) / 2;
+    std::vector<size_t> len(pairs), at(pairs);
     size_t off = 0;
-    for (unsigned r = 0; r < runs; r += 2) {
+    for (unsigned p = 0; p < pairs; ++p) {
+        const unsigned r = 2 * p;
+        len[p] = run_lengths[r] + (r + 1 < runs ? run_lengths[r + 1] : 0);
+        at[p] = off;
+        off += len[p];
+    }
+    for (unsigned k = 0; k < pairs; ++k) {
+        const unsigned p = (first_pair + k) % pairs;
+        const unsigned r = 2 * p;
+        const size_t off = at[p];
         if (r + 1 < runs) {
             rsort_status st = rsort_merge(key, descending, run_keys[r],
                                           value_bytes ? run_values[r] : nullptr, run_lengths[r],
@@ -675,19 +689,14 @@ rsort_status rsort_merge_segments(rsort_key_t key, int descending, unsigned runs
                                           value_bytes ? ov + off * value_bytes : nullptr,
                                           value_bytes, d_partitions, npartitions, stream);
             if (st != RSORT_OK) return st;
-            len.push_back(run_lengths[r] + run_lengths[r + 1]);
-        } else {
-            if (run_lengths[r]) {
-                cudaError_t e = cudaMemcpyAsync(ok + off * kb, run_keys[r], run_lengths[r] * kb,
-                                                cudaMemcpyDeviceToDevice, s);
-                if (e == cudaSuccess && value_bytes)
-                    e = cudaMemcpyAsync(ov + off * value_bytes, run_values[r],
-                                        run_lengths[r] * value_bytes, cudaMemcpyDeviceToDevice, s);
-                if (e != cudaSuccess) return cuda_fail(e, "merge run copy");
-            }
-            len.push_back(run_lengths[r]);
+        } else if (run_lengths[r]) {
+            cudaError_t e = cudaMemcpyAsync(ok + off * kb, run_keys[r], run_lengths[r] * kb,
+                                            cudaMemcpyDeviceToDevice, s);
+            if (e == cudaSuccess && value_bytes)
+                e = cudaMemcpyAsync(ov + off * value_bytes, run_values[r],
+                                    run_lengths[r] * value_bytes, cudaMemcpyDeviceToDevice, s);
+            if (e != cudaSuccess) return cuda_fail(e, "merge run copy");
         }
-        off += len.back();
     }
     if (len.size() <= 1) return RSORT_OK;
     // Later rounds in local memory, between out and scratch.

@@ -329,7 +329,7 @@ class PeerExchange:
             key_code(keys.dtype), int(descending), world, kp, vp, lens, vb, out_k.data_ptr(),
             None if out_v is None else out_v.data_ptr(), sk.data_ptr(),
             None if sv is None else sv.data_ptr(), parts.data_ptr(), nparts,
-            ctypes.byref(in_scratch), stream))
+            ctypes.byref(in_scratch), rank // 2, stream))
         return (sk, sv) if in_scratch.value else (out_k, out_v)
 
     def close(self) -> None:

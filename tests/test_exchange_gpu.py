@@ -90,14 +90,16 @@ def test_merge_segments_matches_merge_runs(runs, desc):
     s2k, s2v = torch.empty_like(ck), torch.empty_like(cv)
     kp = (ctypes.c_void_p * runs)(*[k.data_ptr() if k.numel() else None for k in ks])
     vp = (ctypes.c_void_p * runs)(*[v.data_ptr() if v.numel() else None for v in vs])
-    flag2 = ctypes.c_int(0)
-    raise_for(lib.rsort_merge_segments(kt, int(desc), runs, kp, vp, (ctypes.c_size_t * runs)(*lens),
-                                       4, ok.data_ptr(), ov.data_ptr(), s2k.data_ptr(),
-                                       s2v.data_ptr(), parts.data_ptr(), nparts,
-                                       ctypes.byref(flag2), st))
-    gk, gv = (s2k, s2v) if flag2.value else (ok, ov)
-    torch.cuda.synchronize()
-    assert torch.equal(gk, ek) and torch.equal(gv, ev)
+    for first_pair in range((runs + 1) // 2 + 1):  # launch order must not matter
+        flag2 = ctypes.c_int(0)
+        raise_for(lib.rsort_merge_segments(kt, int(desc), runs, kp, vp,
+                                           (ctypes.c_size_t * runs)(*lens), 4, ok.data_ptr(),
+                                           ov.data_ptr(), s2k.data_ptr(), s2v.data_ptr(),
+                                           parts.data_ptr(), nparts, ctypes.byref(flag2),
+                                           first_pair, st))
+        gk, gv = (s2k, s2v) if flag2.value else (ok, ov)
+        torch.cuda.synchronize()
+        assert torch.equal(gk, ek) and torch.equal(gv, ev)
     # stable: equal keys keep run order, i.e. ascending original index
     k = gk.cpu().numpy().view(np.uint64)
     v = gv.cpu().numpy()
