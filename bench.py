@@ -445,8 +445,12 @@ def run_e2e(args, workload: Workload, keys_h, values_h, dev):
             # descending entry point through the same temporary-allocating path.
             from rccl_b200 import cub
             launch = execution.launch
-            ws = cub.device_radix_sort_workspace(launch, dk.dtype, dk.numel())
-            cub.device_radix_sort_keys_descending(launch, dk, ws)
+            if dv is None:
+                ws = cub.device_radix_sort_workspace(launch, dk.dtype, dk.numel())
+                cub.device_radix_sort_keys_descending(launch, dk, ws)
+            else:
+                ws = cub.device_radix_sort_pairs_workspace(launch, dk.dtype, dv.dtype, dk.numel())
+                cub.device_radix_sort_pairs_descending(launch, dk, dv, ws)
             stream.synchronize()
         elif dv is None:
             thrust.sort(execution, dk)
@@ -471,7 +475,12 @@ def run_e2e(args, workload: Workload, keys_h, values_h, dev):
     ms = t0.elapsed_time(t1) / steps
     return {"value": workload.n / (ms / 1e3), "unit": UNIT, "ms_per_step": ms,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": h2d, "steps": steps,
-            "api": "rccl_b200.thrust with_values().sort() (temporary allocation + sync per call)"}
+            "api": ({(True, True): "rccl_b200.cub device_radix_sort_keys_descending",
+                     (True, False): "rccl_b200.cub device_radix_sort_pairs_descending",
+                     (False, True): "rccl_b200.thrust sort()",
+                     (False, False): "rccl_b200.thrust with_values().sort()"}[
+                         (bool(workload.desc), values_h is None)]
+                    + " (temporary allocation + sync per call)")}
 
 
 # ---------------------------------------------------------------------------
