@@ -419,27 +419,46 @@ def run_single(args, workload: Workload):
 
 
 def run_e2e(args, workload: Workload, keys_h, values_h, dev):
-    """Public API end to end: pinned H2D, thrust-style sort, D2H of the result."""
+    """Public API end to end, as a streaming pipeline: every step copies its
+    input from pinned host memory, sorts it through the public API and copies
+    the result back to pinned host memory.  Three device input buffers let
+    step i+1's upload overlap step i's sort and download (PCIe is full
+    duplex) without waiting for step i-1's download."""
     import torch
     from rccl_b200 import thrust
 
     execution = thrust.Program.load(dev).par()
     stream = execution.stream
+    in_s = torch.cuda.Stream(dev)
+    out_s = torch.cuda.Stream(dev)
     hk = torch.from_numpy(keys_h).pin_memory()
     ok_ = torch.empty_like(hk).pin_memory()
-    dk = torch.empty(hk.shape, dtype=hk.dtype, device=dev)
-    hv = ov = dv = None
+    NB = 3
+    dks = [torch.empty(hk.shape, dtype=hk.dtype, device=dev) for _ in range(NB)]
+    hv = ov = None
+    dvs = [None] * NB
     if values_h is not None:
         hv = torch.from_numpy(values_h).pin_memory()
         ov = torch.empty_like(hv).pin_memory()
-        dv = torch.empty(hv.shape, dtype=hv.dtype, device=dev)
+        dvs = [torch.empty(hv.shape, dtype=hv.dtype, device=dev) for _ in range(NB)]
     h2d = hk.numel() * hk.element_size() + (hv.numel() * hv.element_size() if hv is not None else 0)
+    uploaded = [torch.cuda.Event() for _ in range(NB)]
+    sorted_ = [torch.cuda.Event() for _ in range(NB)]
+    downloaded = [torch.cuda.Event() for _ in range(NB)]
 
-    def step():
-        with torch.cuda.stream(stream):
-            dk.copy_(hk, non_blocking=True)
-            if dv is not None:
-                dv.copy_(hv, non_blocking=True)
+    def upload(i):
+        b = i % NB
+        in_s.wait_event(downloaded[b])  # the buffer's previous result is out
+        with torch.cuda.stream(in_s):
+            dks[b].copy_(hk, non_blocking=True)
+            if hv is not None:
+                dvs[b].copy_(hv, non_blocking=True)
+        uploaded[b].record(in_s)
+
+    def sort(i):
+        b = i % NB
+        dk, dv = dks[b], dvs[b]
+        stream.wait_event(uploaded[b])
         if workload.desc:
             # rccl-thrust has no comparator-free descending sort; use the CUB
             # descending entry point through the same temporary-allocating path.
@@ -456,25 +475,43 @@ def run_e2e(args, workload: Workload, keys_h, values_h, dev):
             thrust.sort(execution, dk)
         else:
             thrust.with_values(dk, dv).sort(execution)
-        with torch.cuda.stream(stream):
-            ok_.copy_(dk, non_blocking=True)
-            if dv is not None:
-                ov.copy_(dv, non_blocking=True)
+        sorted_[b].record(stream)
 
-    steps = max(1, min(args.steps, 5))
-    for _ in range(min(args.warmup, 2)):
-        step()
-    torch.cuda.synchronize()
+    def download(i):
+        b = i % NB
+        out_s.wait_event(sorted_[b])
+        with torch.cuda.stream(out_s):
+            ok_.copy_(dks[b], non_blocking=True)
+            if ov is not None:
+                ov.copy_(dvs[b], non_blocking=True)
+        downloaded[b].record(out_s)
+
+    def pipeline(steps, t0=None, t1=None):
+        if t0 is not None:
+            t0.record(in_s)
+        upload(0)
+        for i in range(steps):
+            if i + 1 < steps:
+                upload(i + 1)
+            sort(i)
+            download(i)
+        if t1 is not None:
+            t1.record(out_s)
+        torch.cuda.synchronize()
+
+    steps = max(3, min(args.steps, 6))
+    pipeline(3)  # warm-up
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for _ in range(steps):
-        step()
-    t1.record(stream)
-    torch.cuda.synchronize()
+    pipeline(steps, t0, t1)
     ms = t0.elapsed_time(t1) / steps
+    # every step's output went through the same host buffer: check the last
+    img = order_image(ok_.numpy(), workload.desc)
+    ok = bool(np.all(img[1:] >= img[:-1]))
     return {"value": workload.n / (ms / 1e3), "unit": UNIT, "ms_per_step": ms,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": h2d, "steps": steps,
+            "output_checked": ok,
+            "pipelined": "step i+1's upload overlaps step i's sort and download",
             "api": ({(True, True): "rccl_b200.cub device_radix_sort_keys_descending",
                      (True, False): "rccl_b200.cub device_radix_sort_pairs_descending",
                      (False, True): "rccl_b200.thrust sort()",
@@ -596,16 +633,24 @@ def run_dist(args, workload: Workload):
                         device=dev)
     del out, ok_k, ok_v
 
-    # End to end through the public API: pinned host shard -> device, sample
-    # sort, this rank's sorted part -> pinned host.
+    # End to end through the public API, as a streaming pipeline: every step
+    # copies the pinned host shard to the device, sample-sorts it and copies
+    # this rank's sorted part back to pinned host memory; three device input
+    # buffers let step i+1's upload overlap step i's sort and download.
     e2e_ms, h2d, d2h = None, 0, 0
     if not args.no_e2e:
         hk = torch.from_numpy(keys_h).pin_memory()
         hv = src_v.cpu().pin_memory() if src_v is not None else None
         h2d = hk.numel() * hk.element_size() + (hv.numel() * hv.element_size() if hv is not None else 0)
-        e2e_steps = max(1, min(args.steps, 3))
-        times = []
+        NB = 3
+        in_s, out_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        dks = [torch.empty_like(hk, device=dev) for _ in range(NB)]
+        dvs = [torch.empty_like(hv, device=dev) if hv is not None else None for _ in range(NB)]
+        uploaded = [torch.cuda.Event() for _ in range(NB)]
+        sorted_ = [torch.cuda.Event() for _ in range(NB)]
+        downloaded = [torch.cuda.Event() for _ in range(NB)]
         pinned = {}
+        out_bytes = [0]
 
         def host_out(t):
             # pinned result buffers, allocated once and grown only if a
@@ -617,33 +662,62 @@ def run_dist(args, workload: Workload):
                 pinned[t.dtype] = buf
             return buf[:t.shape[0]]
 
-        # warm the pinned buffers outside the timed steps
+        def upload(i):
+            b = i % NB
+            in_s.wait_event(downloaded[b])
+            with torch.cuda.stream(in_s):
+                dks[b].copy_(hk, non_blocking=True)
+                if hv is not None:
+                    dvs[b].copy_(hv, non_blocking=True)
+            uploaded[b].record(in_s)
+
+        def sort_and_download(i):
+            b = i % NB
+            torch.cuda.current_stream().wait_event(uploaded[b])
+            rk, rv = D.sample_sort(dks[b], dvs[b], workload.desc, ops=ops)
+            # the step's trailing all-reduce is on this stream: once this event
+            # completes no peer reads the input buffer any more
+            sorted_[b].record()
+            out_s.wait_event(sorted_[b])
+            nb = rk.numel() * rk.element_size()
+            with torch.cuda.stream(out_s):
+                host_out(rk).copy_(rk, non_blocking=True)
+                rk.record_stream(out_s)
+                if rv is not None:
+                    host_out(rv).copy_(rv, non_blocking=True)
+                    rv.record_stream(out_s)
+                    nb += rv.numel() * rv.element_size()
+            downloaded[b].record(out_s)
+            out_bytes[0] = max(out_bytes[0], nb)
+
+        def pipeline(steps, t0=None, t1=None):
+            torch.cuda.synchronize()
+            dist.barrier()
+            if t0 is not None:
+                t0.record(in_s)
+            upload(0)
+            for i in range(steps):
+                if i + 1 < steps:
+                    upload(i + 1)
+                sort_and_download(i)
+            if t1 is not None:
+                t1.record(out_s)
+            torch.cuda.synchronize()
+
+        # warm the pinned buffers and the pipeline outside the timed steps
         host_out(torch.empty(m, dtype=src_k.dtype))
         if src_v is not None:
             host_out(torch.empty(m, dtype=src_v.dtype))
-        for i in range(e2e_steps + 1):
-            torch.cuda.synchronize()
-            dist.barrier()
-            a0 = torch.cuda.Event(enable_timing=True)
-            a1 = torch.cuda.Event(enable_timing=True)
-            a0.record()
-            dk = hk.to(dev, non_blocking=True)
-            dv = hv.to(dev, non_blocking=True) if hv is not None else None
-            rk, rv = D.sample_sort(dk, dv, workload.desc, ops=ops)
-            host_out(rk).copy_(rk, non_blocking=True)
-            nb = rk.numel() * rk.element_size()
-            if rv is not None:
-                host_out(rv).copy_(rv, non_blocking=True)
-                nb += rv.numel() * rv.element_size()
-            a1.record()
-            torch.cuda.synchronize()
-            if i > 0:  # first iteration is warm-up
-                times.append(a0.elapsed_time(a1))
-                d2h = max(d2h, nb)
-            del dk, dv, rk, rv
-        tt = torch.tensor(times, dtype=torch.float64, device=dev)
+        e2e_steps = 3
+        pipeline(2)
+        a0 = torch.cuda.Event(enable_timing=True)
+        a1 = torch.cuda.Event(enable_timing=True)
+        pipeline(e2e_steps, a0, a1)
+        d2h = out_bytes[0]
+        tt = torch.tensor([a0.elapsed_time(a1) / e2e_steps], dtype=torch.float64, device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_ms = sum(tt.tolist()) / len(times)
+        e2e_ms = tt.item()
+        del dks, dvs
     dist.barrier()
     if rank == 0:
         total_ms = sum(step_max)
@@ -682,6 +756,7 @@ def run_dist(args, workload: Workload):
             "e2e": None if e2e_ms is None else {
                 "value": world * m / (e2e_ms / 1e3), "unit": UNIT, "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "pipelined": "step i+1's upload overlaps step i's sort and download",
                 "api": "rccl_b200.dist.sample_sort from pinned host shards (max over ranks)"},
         }
         print(json.dumps(line), flush=True)
