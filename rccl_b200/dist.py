@@ -233,7 +233,7 @@ class PeerExchange:
     the NCCL exchange, since all ranks see the same export flags."""
 
     WORDS = 1 + 2 * (_lib.IPC_HANDLE_BYTES // 8 + 1)  # flag, (handle, offset) x 2
-    CACHE = 64
+    CACHE = 256
 
     def __init__(self):
         self._mapped: "OrderedDict[bytes, int]" = OrderedDict()
@@ -265,9 +265,13 @@ class PeerExchange:
             p = ctypes.c_void_p(0)
             raise_for(_lib.lib().rsort_ipc_import(handle, ctypes.byref(p)))
             self._mapped[handle] = p.value
-            while len(self._mapped) > self.CACHE:
-                _, old = self._mapped.popitem(last=False)
-                _lib.lib().rsort_ipc_release(ctypes.c_void_p(old))
+            if len(self._mapped) > self.CACHE:
+                # A kernel of an earlier call may still read the oldest
+                # mappings: let the device drain before unmapping.
+                torch.cuda.synchronize()
+                while len(self._mapped) > self.CACHE:
+                    _, old = self._mapped.popitem(last=False)
+                    _lib.lib().rsort_ipc_release(ctypes.c_void_p(old))
             return p.value
 
     def pull(self, keys, values, out_k, out_v, table, sizes, rank: int, world: int, stream) -> None:
@@ -334,6 +338,8 @@ class PeerExchange:
 
     def close(self) -> None:
         with self._lock:
+            if self._mapped and torch.cuda.is_available():
+                torch.cuda.synchronize()
             while self._mapped:
                 _, p = self._mapped.popitem()
                 _lib.lib().rsort_ipc_release(ctypes.c_void_p(p))
