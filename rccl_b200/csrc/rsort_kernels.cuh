@@ -24,10 +24,10 @@ constexpr int ONESWEEP_THREADS = RSORT_ONESWEEP_THREADS;
 #define RSORT_ITEMS_KEYS32 24
 #endif
 #ifndef RSORT_ITEMS_KEYS64
-#define RSORT_ITEMS_KEYS64 12
+#define RSORT_ITEMS_KEYS64 15
 #endif
 #ifndef RSORT_ITEMS_PAIRS64_32
-#define RSORT_ITEMS_PAIRS64_32 10
+#define RSORT_ITEMS_PAIRS64_32 12
 #endif
 #ifndef RSORT_ITEMS_PAIRS32_32
 #define RSORT_ITEMS_PAIRS32_32 16
