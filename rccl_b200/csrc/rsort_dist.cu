@@ -114,11 +114,14 @@ __global__ void bounds_kernel(const B *keys, uint64_t m, uint32_t rank, const Co
 // binary search on the cross diagonal, stages both segments in shared memory,
 // merges MERGE_ITEMS outputs per thread and writes the tile out coalesced.
 // ---------------------------------------------------------------------------
-constexpr int MERGE_THREADS = 256;
+#ifndef RSORT_MERGE_THREADS
+#define RSORT_MERGE_THREADS 256
+#endif
+constexpr int MERGE_THREADS = RSORT_MERGE_THREADS;
 // Odd, so the serial per-thread merges of neighbouring lanes (which start
 // MERGE_ITEMS items apart in shared memory) fall into different banks.
 #ifndef RSORT_MERGE_ITEMS
-#define RSORT_MERGE_ITEMS 11
+#define RSORT_MERGE_ITEMS 13
 #endif
 constexpr int MERGE_ITEMS = RSORT_MERGE_ITEMS;
 constexpr int MERGE_TILE = MERGE_THREADS * MERGE_ITEMS;
