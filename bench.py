@@ -520,6 +520,83 @@ def run_e2e(args, workload: Workload, keys_h, values_h, dev):
                     + " (temporary allocation + sync per call)")}
 
 
+def run_cub_proxy(args, workload: Workload):
+    """Comparator only: CUB DeviceRadixSort from the toolkit's CCCL headers
+    (baseline/cub_proxy.cu, built here for sm_100a), which the reference's
+    radix path ports, timed on the same inputs the same way as run_single."""
+    import ctypes
+    import torch
+
+    kind = {2: 0, 3: 1}.get(workload.config, 2)
+    if (kind == 0 and (workload.key, workload.value) != (np.uint64, np.uint32)) or \
+            (kind == 1 and workload.key != np.float32) or (kind == 2 and workload.key != np.uint32):
+        print(json.dumps({"impl": "cub-proxy", "unavailable": "no CUB proxy for this workload"}))
+        return
+    src = os.path.join(ROOT, "baseline", "cub_proxy.cu")
+    out_dir = os.path.join(ROOT, "baseline", "_cub")
+    so = os.path.join(out_dir, "libcub_proxy.so")
+    if not os.path.exists(so) or os.path.getmtime(so) < os.path.getmtime(src):
+        os.makedirs(out_dir, exist_ok=True)
+        subprocess.run(["nvcc", "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17",
+                        "-Xcompiler", "-fPIC", "-shared", src, "-o", so], check=True)
+    L = ctypes.CDLL(so)
+    vp, sz = ctypes.c_void_p, ctypes.c_size_t
+    L.cub_proxy_temp_bytes.argtypes = [ctypes.c_int, sz, ctypes.POINTER(sz)]
+    L.cub_proxy_sort.argtypes = [ctypes.c_int, vp, vp, vp, vp, sz, vp, sz,
+                                 ctypes.POINTER(ctypes.c_int), vp]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    keys_h, values_h = workload.generate()
+    src_k = torch.from_numpy(keys_h).to(dev)
+    k0, k1 = torch.empty_like(src_k), torch.empty_like(src_k)
+    src_v = v0 = v1 = None
+    if values_h is not None:
+        src_v = torch.from_numpy(values_h).to(dev)
+        v0, v1 = torch.empty_like(src_v), torch.empty_like(src_v)
+    nbytes = sz(0)
+    assert L.cub_proxy_temp_bytes(kind, workload.n, ctypes.byref(nbytes)) == 0
+    temp = torch.empty(max(nbytes.value, 1), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    sel = ctypes.c_int(0)
+
+    def restore():
+        k0.copy_(src_k)
+        if v0 is not None:
+            v0.copy_(src_v)
+
+    def sort():
+        assert L.cub_proxy_sort(kind, k0.data_ptr(), k1.data_ptr(),
+                                None if v0 is None else v0.data_ptr(),
+                                None if v1 is None else v1.data_ptr(), workload.n,
+                                temp.data_ptr(), nbytes.value, ctypes.byref(sel),
+                                stream.cuda_stream) == 0
+
+    for _ in range(args.warmup):
+        restore()
+        sort()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(args.steps):
+        restore()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        sort()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    out = (k1 if sel.value else k0).cpu().numpy()
+    img = order_image(out, workload.desc)
+    ms = statistics.mean(times)
+    print(json.dumps({
+        "impl": "cub-proxy", "metric": METRIC, "value": workload.n / (ms / 1e3), "unit": UNIT,
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "dtype": np.dtype(workload.key).name,
+        "config": config_dict(args, workload),
+        "cub_version": "CCCL 2.8.2 headers from the CUDA 12.9 toolkit, nvcc -arch=sm_100a",
+        "output_sorted": bool(np.all(img[1:] >= img[:-1]))}), flush=True)
+
+
 # ---------------------------------------------------------------------------
 # N GPUs: distributed sample sort, one process per GPU (weak scaling: every
 # rank holds one workload-sized contiguous shard of the global input)
@@ -775,12 +852,17 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the end-to-end leg (used for profiler runs)")
+    ap.add_argument("--cub-proxy", action="store_true",
+                    help="time CUB DeviceRadixSort (toolkit headers) on the same workload instead")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     workload = Workload(args.config, args.n)
     if args.impl == "reference":
         run_reference(args, workload, rank)
+        return
+    if args.cub_proxy:
+        run_cub_proxy(args, workload)
         return
     if world > 1 or args.gpus > 1:
         run_dist(args, workload)
