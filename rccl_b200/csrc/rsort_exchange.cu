@@ -1,11 +1,13 @@
 // Bucket exchange of the multi-GPU sample sort over NVLink peer memory (no
 // reference counterpart: the reference is single-GPU).
 //
-// Each rank exports its sorted shard (keys, values) with CUDA IPC; every peer
-// maps it once and PULLS its own bucket straight out of the shard with
-// rsort_gather_segments, an SM-driven copy kernel reading the peers' HBM over
-// NVLink / NVSwitch.  This replaces the NCCL send/recv exchange: no staging
-// buffers, no proxy copies, and every peer is read at the same time.
+// Each rank exports its sorted shard (keys, values) with CUDA IPC and every
+// peer maps it once.  The default exchange then merges the buckets straight
+// out of the peers' shards (rsort_merge_segments); the "peer-copy" exchange
+// instead PULLS every bucket with rsort_gather_segments, the SM-driven copy
+// kernel below reading the peers' HBM over NVLink / NVSwitch, all peers at
+// the same time, with no staging buffers or proxy copies.  Also here: the
+// allocation-base lookup that CUDA IPC export needs.
 //
 // The kernel waits on nothing: the caller orders it after the peers' sorts
 // (a collective that every rank enters after its own sort) and orders the
