@@ -212,6 +212,49 @@ rsort_status rsort_merge_segments(rsort_key_t key, int descending, unsigned runs
                                   rsort_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * DeviceMergeSort / DeviceMerge for named orders.
+ *
+ * rccl-cub's merge sort and merge (rccl-cub/src/dispatch.rs:170-193,
+ * 1572-1601; the Thrust sort_by / sort_unstable_by lowering,
+ * rccl-thrust/src/backend.rs:39-63, 112-150) take a comparator closure
+ * compiled to device code, which a C ABI cannot carry.  These entry points
+ * take the comparators such closures almost always are:
+ *   RSORT_ORDER_ASCENDING        |a, b| a.cmp(b); floats a.partial_cmp(b),
+ *                                -0.0 == +0.0 (the radix order)
+ *   RSORT_ORDER_DESCENDING       |a, b| b.cmp(a)
+ *   RSORT_ORDER_TOTAL_ASCENDING  |a, b| a.total_cmp(b): -0.0 < +0.0, NaNs by
+ *                                sign and payload (integers: as ASCENDING)
+ *   RSORT_ORDER_TOTAL_DESCENDING |a, b| b.total_cmp(a)
+ * The sorts are stable, like rccl-cub's merge sort, so their output equals
+ * the comparator sort's for these orders; they run on the radix path (no
+ * comparisons), with the radix workspace (rsort_controls_query) and
+ * scratch, result in place.  rsort_merge_ordered merges two sorted runs
+ * (ties: a first) with rsort_merge's partitions.
+ * ------------------------------------------------------------------------- */
+typedef enum {
+    RSORT_ORDER_ASCENDING = 0,
+    RSORT_ORDER_DESCENDING = 1,
+    RSORT_ORDER_TOTAL_ASCENDING = 2,
+    RSORT_ORDER_TOTAL_DESCENDING = 3
+} rsort_order_t;
+
+rsort_status rsort_merge_sort_keys(rsort_key_t key, rsort_order_t order, void *d_keys,
+                                   void *d_scratch, size_t nscratch, size_t n, uint64_t *bins,
+                                   size_t nbins, int32_t *lookback, size_t nlookback,
+                                   int32_t *counters, size_t ncounters, rsort_stream_t stream);
+rsort_status rsort_merge_sort_pairs(rsort_key_t key, rsort_order_t order, void *d_keys,
+                                    void *d_values, size_t value_bytes, void *d_scratch_keys,
+                                    size_t nscratch_keys, void *d_scratch_values,
+                                    size_t nscratch_values, size_t n, uint64_t *bins, size_t nbins,
+                                    int32_t *lookback, size_t nlookback, int32_t *counters,
+                                    size_t ncounters, rsort_stream_t stream);
+rsort_status rsort_merge_ordered(rsort_key_t key, rsort_order_t order, const void *a_keys,
+                                 const void *a_values, size_t na, const void *b_keys,
+                                 const void *b_values, size_t nb, void *out_keys,
+                                 void *out_values, size_t value_bytes, uint64_t *d_partitions,
+                                 size_t npartitions, rsort_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Bucket exchange over NVLink peer memory (no reference counterpart).
  *
  * Replaces step 5 above (the NCCL all-to-all): every rank exports its sorted

@@ -206,6 +206,55 @@ inline void device_radix_sort_pairs_buffer_descending(cudaStream_t stream,
     device_radix_sort_pairs_buffer_impl(stream, b, begin, end, ws, 1);
 }
 
+// --- DeviceMergeSort / DeviceMerge for named orders -------------------------
+// (rccl-cub dispatch.rs:170-193, 1113-1146, 1570-1601 take a comparator
+// closure; here the comparator is one of the named orders of rsort_order_t.)
+enum class Order : int {
+    Ascending = RSORT_ORDER_ASCENDING,
+    Descending = RSORT_ORDER_DESCENDING,
+    TotalAscending = RSORT_ORDER_TOTAL_ASCENDING,
+    TotalDescending = RSORT_ORDER_TOTAL_DESCENDING,
+};
+
+template <typename K>
+inline void device_merge_sort_keys(cudaStream_t stream, K *keys, K *scratch, size_t n,
+                                   const DeviceRadixSortBufferWorkspace &ws, Order order) {
+    check(rsort_merge_sort_keys(RadixKey<K>::code, static_cast<rsort_order_t>(order), keys,
+                                scratch, n, n, ws.bins, ws.nbins, ws.lookback, ws.nlookback,
+                                ws.counters, ws.ncounters, reinterpret_cast<rsort_stream_t>(stream)));
+}
+
+template <typename K, typename V>
+inline void device_merge_sort_pairs(cudaStream_t stream, K *keys, V *values, K *scratch_keys,
+                                    V *scratch_values, size_t n,
+                                    const DeviceRadixSortBufferWorkspace &ws, Order order) {
+    check(rsort_merge_sort_pairs(RadixKey<K>::code, static_cast<rsort_order_t>(order), keys,
+                                 values, sizeof(V), scratch_keys, n, scratch_values, n, n, ws.bins,
+                                 ws.nbins, ws.lookback, ws.nlookback, ws.counters, ws.ncounters,
+                                 reinterpret_cast<rsort_stream_t>(stream)));
+}
+
+// d_partitions: rsort_merge_partition_words(na + nb) words.
+template <typename K>
+inline void device_merge_keys(cudaStream_t stream, const K *first, size_t na, const K *second,
+                              size_t nb, uint64_t *d_partitions, size_t npartitions, K *output,
+                              Order order) {
+    check(rsort_merge_ordered(RadixKey<K>::code, static_cast<rsort_order_t>(order), first, nullptr,
+                              na, second, nullptr, nb, output, nullptr, 0, d_partitions,
+                              npartitions, reinterpret_cast<rsort_stream_t>(stream)));
+}
+
+template <typename K, typename V>
+inline void device_merge_pairs(cudaStream_t stream, const K *first_keys, const V *first_values,
+                               size_t na, const K *second_keys, const V *second_values, size_t nb,
+                               uint64_t *d_partitions, size_t npartitions, K *output_keys,
+                               V *output_values, Order order) {
+    check(rsort_merge_ordered(RadixKey<K>::code, static_cast<rsort_order_t>(order), first_keys,
+                              first_values, na, second_keys, second_values, nb, output_keys,
+                              output_values, sizeof(V), d_partitions, npartitions,
+                              reinterpret_cast<rsort_stream_t>(stream)));
+}
+
 }  // namespace cub
 }  // namespace rccl_b200
 

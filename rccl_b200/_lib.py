@@ -60,6 +60,9 @@ EXPORTED_SYMBOLS = (
     "rsort_ipc_release",
     "rsort_gather_segments",
     "rsort_merge_segments",
+    "rsort_merge_sort_keys",
+    "rsort_merge_sort_pairs",
+    "rsort_merge_ordered",
 )
 
 
@@ -141,6 +144,13 @@ def _declare(lib: ctypes.CDLL) -> None:
                                          ctypes.POINTER(sz), sz, vp, vp, vp, vp, vp, sz, pi, u,
                                          vp]
     lib.rsort_merge_segments.restype = i
+    lib.rsort_merge_sort_keys.argtypes = [i, i, vp, vp, sz, sz, vp, sz, vp, sz, vp, sz, vp]
+    lib.rsort_merge_sort_keys.restype = i
+    lib.rsort_merge_sort_pairs.argtypes = [i, i, vp, vp, sz, vp, sz, vp, sz, sz, vp, sz, vp, sz,
+                                           vp, sz, vp]
+    lib.rsort_merge_sort_pairs.restype = i
+    lib.rsort_merge_ordered.argtypes = [i, i, vp, vp, sz, vp, vp, sz, vp, vp, sz, vp, sz, vp]
+    lib.rsort_merge_ordered.restype = i
 
 
 def lib() -> ctypes.CDLL:

@@ -163,9 +163,12 @@ rsort_status validate_controls(const Controls &c, size_t n, int kb, int vb) {
 }
 
 // One sort over a DoubleBuffer.  values == nullptr pointers for keys-only.
+// total: float keys in IEEE total order (no zero fold; the named-order merge
+// sort entry points), else the reference's radix order.
 rsort_status sort_buffer(rsort_key_t key, int descending, void *kf, void *ks, void *vf, void *vs,
                          size_t vb, size_t n, unsigned begin_bit, unsigned end_bit,
-                         int *current_is_first, const Controls &c, cudaStream_t stream) {
+                         int *current_is_first, const Controls &c, cudaStream_t stream,
+                         bool total = false) {
     if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
     if (!value_ok(vb)) return fail(RSORT_BAD_ARGUMENT, "radix value width");
     if (!current_is_first) return fail(RSORT_BAD_ARGUMENT, "null selector");
@@ -182,7 +185,7 @@ rsort_status sort_buffer(rsort_key_t key, int descending, void *kf, void *ks, vo
     void *kout = cur_first ? ks : kf;
     void *vin = cur_first ? vf : vs;
     void *vout = cur_first ? vs : vf;
-    const int kind = key_kind(key);
+    const int kind = total && key_kind(key) == KIND_FLOAT ? KIND_FLOAT_TOTAL : key_kind(key);
 
     // rccl-cub/src/radix.rs:470-492: single-tile route, one selector flip.
     DeviceInfo dev;
@@ -312,28 +315,26 @@ rsort_status rsort_pairs_buffer(rsort_key_t key, int descending, void *d_keys_fi
                        reinterpret_cast<cudaStream_t>(stream));
 }
 
-rsort_status rsort_keys(rsort_key_t key, int descending, void *d_keys, void *d_scratch,
-                        size_t nscratch, size_t n, uint64_t *bins, size_t nbins, int32_t *lookback,
-                        size_t nlookback, int32_t *counters, size_t ncounters,
-                        rsort_stream_t stream) {
+namespace {
+
+rsort_status keys_in_place(rsort_key_t key, int descending, bool total, void *d_keys,
+                           void *d_scratch, size_t nscratch, size_t n, const Controls &c,
+                           cudaStream_t s) {
     if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
     // rccl-cub/src/radix.rs:591-600
     if (nscratch != n) return fail(RSORT_LENGTH_MISMATCH, "radix scratch keys", n, nscratch);
     const int kb = key_bytes(key);
-    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     if (n > 0 && single_route(n, kb, 0)) {
         // The single-tile kernel reads its whole input before writing, so it
         // sorts in place and the reference's copy-back (radix.rs:617-621) is
         // not needed.
         int sel = 0;
-        Controls c{bins, nbins, lookback, nlookback, counters, ncounters};
         return sort_buffer(key, descending, d_keys, d_keys, nullptr, nullptr, 0, n, 0,
-                           unsigned(kb) * 8, &sel, c, s);
+                           unsigned(kb) * 8, &sel, c, s, total);
     }
     int current_is_first = 1;
-    Controls c{bins, nbins, lookback, nlookback, counters, ncounters};
     rsort_status st = sort_buffer(key, descending, d_keys, d_scratch, nullptr, nullptr, 0, n, 0,
-                                  unsigned(kb) * 8, &current_is_first, c, s);
+                                  unsigned(kb) * 8, &current_is_first, c, s, total);
     if (st != RSORT_OK) return st;
     if (!current_is_first && n > 0) {
         cudaError_t e = cudaMemcpyAsync(d_keys, d_scratch, n * size_t(kb), cudaMemcpyDeviceToDevice, s);
@@ -342,11 +343,10 @@ rsort_status rsort_keys(rsort_key_t key, int descending, void *d_keys, void *d_s
     return RSORT_OK;
 }
 
-rsort_status rsort_pairs(rsort_key_t key, int descending, void *d_keys, void *d_values,
-                         size_t value_bytes, void *d_scratch_keys, size_t nscratch_keys,
-                         void *d_scratch_values, size_t nscratch_values, size_t n, uint64_t *bins,
-                         size_t nbins, int32_t *lookback, size_t nlookback, int32_t *counters,
-                         size_t ncounters, rsort_stream_t stream) {
+rsort_status pairs_in_place(rsort_key_t key, int descending, bool total, void *d_keys,
+                            void *d_values, size_t value_bytes, void *d_scratch_keys,
+                            size_t nscratch_keys, void *d_scratch_values, size_t nscratch_values,
+                            size_t n, const Controls &c, cudaStream_t s) {
     if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
     if (value_bytes == 0 || !value_ok(value_bytes))
         return fail(RSORT_BAD_ARGUMENT, "radix value width");
@@ -355,17 +355,15 @@ rsort_status rsort_pairs(rsort_key_t key, int descending, void *d_keys, void *d_
     if (nscratch_values != n)
         return fail(RSORT_LENGTH_MISMATCH, "radix scratch values", n, nscratch_values);
     const int kb = key_bytes(key);
-    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    Controls c{bins, nbins, lookback, nlookback, counters, ncounters};
     if (n > 0 && single_route(n, kb, int(value_bytes))) {
         int sel = 0;
         return sort_buffer(key, descending, d_keys, d_keys, d_values, d_values, value_bytes, n, 0,
-                           unsigned(kb) * 8, &sel, c, s);
+                           unsigned(kb) * 8, &sel, c, s, total);
     }
     int current_is_first = 1;
     rsort_status st = sort_buffer(key, descending, d_keys, d_scratch_keys, d_values,
                                   d_scratch_values, value_bytes, n, 0, unsigned(kb) * 8,
-                                  &current_is_first, c, s);
+                                  &current_is_first, c, s, total);
     if (st != RSORT_OK) return st;
     if (!current_is_first && n > 0) {
         cudaError_t e = cudaMemcpyAsync(d_keys, d_scratch_keys, n * size_t(kb),
@@ -376,6 +374,59 @@ rsort_status rsort_pairs(rsort_key_t key, int descending, void *d_keys, void *d_
         if (e != cudaSuccess) return cuda_fail(e, "copy back");
     }
     return RSORT_OK;
+}
+
+bool order_ok(rsort_order_t o) { return int(o) >= 0 && int(o) <= 3; }
+bool order_desc(rsort_order_t o) {
+    return o == RSORT_ORDER_DESCENDING || o == RSORT_ORDER_TOTAL_DESCENDING;
+}
+bool order_total(rsort_order_t o) {
+    return o == RSORT_ORDER_TOTAL_ASCENDING || o == RSORT_ORDER_TOTAL_DESCENDING;
+}
+
+}  // namespace
+
+rsort_status rsort_keys(rsort_key_t key, int descending, void *d_keys, void *d_scratch,
+                        size_t nscratch, size_t n, uint64_t *bins, size_t nbins, int32_t *lookback,
+                        size_t nlookback, int32_t *counters, size_t ncounters,
+                        rsort_stream_t stream) {
+    Controls c{bins, nbins, lookback, nlookback, counters, ncounters};
+    return keys_in_place(key, descending, false, d_keys, d_scratch, nscratch, n, c,
+                         reinterpret_cast<cudaStream_t>(stream));
+}
+
+rsort_status rsort_merge_sort_keys(rsort_key_t key, rsort_order_t order, void *d_keys,
+                                   void *d_scratch, size_t nscratch, size_t n, uint64_t *bins,
+                                   size_t nbins, int32_t *lookback, size_t nlookback,
+                                   int32_t *counters, size_t ncounters, rsort_stream_t stream) {
+    if (!order_ok(order)) return fail(RSORT_BAD_ARGUMENT, "sort order");
+    Controls c{bins, nbins, lookback, nlookback, counters, ncounters};
+    return keys_in_place(key, order_desc(order) ? 1 : 0, order_total(order), d_keys, d_scratch,
+                         nscratch, n, c, reinterpret_cast<cudaStream_t>(stream));
+}
+
+rsort_status rsort_pairs(rsort_key_t key, int descending, void *d_keys, void *d_values,
+                         size_t value_bytes, void *d_scratch_keys, size_t nscratch_keys,
+                         void *d_scratch_values, size_t nscratch_values, size_t n, uint64_t *bins,
+                         size_t nbins, int32_t *lookback, size_t nlookback, int32_t *counters,
+                         size_t ncounters, rsort_stream_t stream) {
+    Controls c{bins, nbins, lookback, nlookback, counters, ncounters};
+    return pairs_in_place(key, descending, false, d_keys, d_values, value_bytes, d_scratch_keys,
+                          nscratch_keys, d_scratch_values, nscratch_values, n, c,
+                          reinterpret_cast<cudaStream_t>(stream));
+}
+
+rsort_status rsort_merge_sort_pairs(rsort_key_t key, rsort_order_t order, void *d_keys,
+                                    void *d_values, size_t value_bytes, void *d_scratch_keys,
+                                    size_t nscratch_keys, void *d_scratch_values,
+                                    size_t nscratch_values, size_t n, uint64_t *bins, size_t nbins,
+                                    int32_t *lookback, size_t nlookback, int32_t *counters,
+                                    size_t ncounters, rsort_stream_t stream) {
+    if (!order_ok(order)) return fail(RSORT_BAD_ARGUMENT, "sort order");
+    Controls c{bins, nbins, lookback, nlookback, counters, ncounters};
+    return pairs_in_place(key, order_desc(order) ? 1 : 0, order_total(order), d_keys, d_values,
+                          value_bytes, d_scratch_keys, nscratch_keys, d_scratch_values,
+                          nscratch_values, n, c, reinterpret_cast<cudaStream_t>(stream));
 }
 
 rsort_status rsort_check_device_status(int32_t *counters, size_t ncounters,
@@ -563,10 +614,37 @@ rsort_status rsort_gather_segments(unsigned nseg, const void *const *d_src, cons
 
 size_t rsort_merge_partition_words(size_t total) { return merge_partition_words(total, 0); }
 
+namespace {
+rsort_status merge_impl(rsort_key_t key, int descending, bool total, const void *a_keys,
+                        const void *a_values, size_t na, const void *b_keys, const void *b_values,
+                        size_t nb, void *out_keys, void *out_values, size_t value_bytes,
+                        uint64_t *d_partitions, size_t npartitions, rsort_stream_t stream);
+}
+
 rsort_status rsort_merge(rsort_key_t key, int descending, const void *a_keys,
                          const void *a_values, size_t na, const void *b_keys, const void *b_values,
                          size_t nb, void *out_keys, void *out_values, size_t value_bytes,
                          uint64_t *d_partitions, size_t npartitions, rsort_stream_t stream) {
+    return merge_impl(key, descending, false, a_keys, a_values, na, b_keys, b_values, nb, out_keys,
+                      out_values, value_bytes, d_partitions, npartitions, stream);
+}
+
+rsort_status rsort_merge_ordered(rsort_key_t key, rsort_order_t order, const void *a_keys,
+                                 const void *a_values, size_t na, const void *b_keys,
+                                 const void *b_values, size_t nb, void *out_keys,
+                                 void *out_values, size_t value_bytes, uint64_t *d_partitions,
+                                 size_t npartitions, rsort_stream_t stream) {
+    if (!order_ok(order)) return fail(RSORT_BAD_ARGUMENT, "sort order");
+    return merge_impl(key, order_desc(order) ? 1 : 0, order_total(order), a_keys, a_values, na,
+                      b_keys, b_values, nb, out_keys, out_values, value_bytes, d_partitions,
+                      npartitions, stream);
+}
+
+namespace {
+rsort_status merge_impl(rsort_key_t key, int descending, bool total, const void *a_keys,
+                        const void *a_values, size_t na, const void *b_keys, const void *b_values,
+                        size_t nb, void *out_keys, void *out_values, size_t value_bytes,
+                        uint64_t *d_partitions, size_t npartitions, rsort_stream_t stream) {
     if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
     if (!value_ok(value_bytes)) return fail(RSORT_BAD_ARGUMENT, "radix value width");
     if (na + nb == 0) return RSORT_OK;
@@ -581,8 +659,9 @@ rsort_status rsort_merge(rsort_key_t key, int descending, const void *a_keys,
     rsort_status st = device_info(&dev);
     if (st != RSORT_OK) return st;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    MergeArgs p{a_keys, a_values, na, b_keys, b_values, nb, out_keys, out_values,
-                key_kind(key), descending ? 1 : 0};
+    const int kind = total && key_kind(key) == KIND_FLOAT ? KIND_FLOAT_TOTAL : key_kind(key);
+    MergeArgs p{a_keys, a_values, na, b_keys, b_values, nb, out_keys, out_values, kind,
+                descending ? 1 : 0};
     cudaError_t e;
     {
         LaunchScope scope(RSORT_KERNEL_MERGE, s);
@@ -590,6 +669,7 @@ rsort_status rsort_merge(rsort_key_t key, int descending, const void *a_keys,
     }
     return e == cudaSuccess ? RSORT_OK : cuda_fail(e, "merge launch");
 }
+}  // namespace
 
 rsort_status rsort_merge_runs(rsort_key_t key, int descending, void *keys, void *values,
                               size_t value_bytes, const size_t *run_lengths, unsigned runs,

@@ -9,7 +9,15 @@
 
 namespace rsort {
 
-enum KeyKind : int { KIND_UINT = 0, KIND_SINT = 1, KIND_FLOAT = 2 };
+// KIND_FLOAT_TOTAL: float keys in IEEE total order (Rust's total_cmp): the
+// float bit transform without the zero fold, so -0.0 sorts before +0.0.  It
+// serves the named-order merge sort entry points; the radix entry points use
+// KIND_FLOAT (the reference's radix order, where -0.0 and +0.0 are equal).
+enum KeyKind : int { KIND_UINT = 0, KIND_SINT = 1, KIND_FLOAT = 2, KIND_FLOAT_TOTAL = 3 };
+
+__host__ __device__ constexpr bool is_float_kind(int kind) {
+    return kind == KIND_FLOAT || kind == KIND_FLOAT_TOTAL;
+}
 
 constexpr int RADIX = 256;
 constexpr uint32_t INVALID_DIGIT = 256;
@@ -44,7 +52,7 @@ template <typename B>
 __device__ __forceinline__ B to_ordered(B raw, KeyXform x) {
     using T = KeyBits<B>;
     B o = raw;
-    if (x.kind == KIND_FLOAT) {
+    if (is_float_kind(x.kind)) {
         o ^= B(typename T::Signed(raw) >> (T::WIDTH - 1)) | T::SIGN;
     } else if (x.kind == KIND_SINT) {
         o ^= T::SIGN;
@@ -56,7 +64,7 @@ template <typename B>
 __device__ __forceinline__ B from_ordered(B ordered, KeyXform x) {
     using T = KeyBits<B>;
     B a = x.desc ? B(~ordered) : ordered;
-    if (x.kind == KIND_FLOAT) {
+    if (is_float_kind(x.kind)) {
         // top bit set -> was non-negative: flip the sign bit; else flip all bits
         a ^= (a & T::SIGN) ? T::SIGN : B(~B(0));
     } else if (x.kind == KIND_SINT) {
@@ -70,7 +78,7 @@ __device__ __forceinline__ B from_ordered(B ordered, KeyXform x) {
 template <int KIND, typename B>
 __device__ __forceinline__ B to_ordered_k(B raw, B dmask) {
     using T = KeyBits<B>;
-    if constexpr (KIND == KIND_FLOAT)
+    if constexpr (is_float_kind(KIND))
         return raw ^ (B(typename T::Signed(raw) >> (T::WIDTH - 1)) | T::SIGN) ^ dmask;
     else if constexpr (KIND == KIND_SINT)
         return raw ^ T::SIGN ^ dmask;
@@ -82,7 +90,7 @@ template <int KIND, typename B>
 __device__ __forceinline__ B from_ordered_k(B ordered, B dmask) {
     using T = KeyBits<B>;
     const B a = ordered ^ dmask;
-    if constexpr (KIND == KIND_FLOAT)
+    if constexpr (is_float_kind(KIND))
         return a ^ (T::SIGN | B(~B(typename T::Signed(a) >> (T::WIDTH - 1))));
     else if constexpr (KIND == KIND_SINT)
         return a ^ T::SIGN;

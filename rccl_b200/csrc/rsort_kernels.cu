@@ -654,9 +654,10 @@ cudaError_t onesweep_t(const PassArgs &a, uint64_t tiles, cudaStream_t s) {
     constexpr int ITEMS = onesweep_items(int(sizeof(B)), VB);
     using L = OnesweepSmem<B, VB, ITEMS>;
     constexpr bool P = sizeof(B) == 8;
-    auto k = a.kind == KIND_FLOAT  ? onesweep_kernel<B, VB, ITEMS, KIND_FLOAT, P>
-             : a.kind == KIND_SINT ? onesweep_kernel<B, VB, ITEMS, KIND_SINT, P>
-                                   : onesweep_kernel<B, VB, ITEMS, KIND_UINT, P>;
+    auto k = a.kind == KIND_FLOAT         ? onesweep_kernel<B, VB, ITEMS, KIND_FLOAT, P>
+             : a.kind == KIND_FLOAT_TOTAL ? onesweep_kernel<B, VB, ITEMS, KIND_FLOAT_TOTAL, P>
+             : a.kind == KIND_SINT        ? onesweep_kernel<B, VB, ITEMS, KIND_SINT, P>
+                                          : onesweep_kernel<B, VB, ITEMS, KIND_UINT, P>;
     cudaError_t e = ensure_smem(k, L::BYTES);
     if (e != cudaSuccess) return e;
     if (!P) {
@@ -743,6 +744,7 @@ static cudaError_t histogram_kind(const HistArgs &a, int blocks, cudaStream_t st
     switch (a.kind) {
         case KIND_SINT: return histogram_full<B, KIND_SINT>(a, blocks, stream);
         case KIND_FLOAT: return histogram_full<B, KIND_FLOAT>(a, blocks, stream);
+        case KIND_FLOAT_TOTAL: return histogram_full<B, KIND_FLOAT_TOTAL>(a, blocks, stream);
         default: return histogram_full<B, KIND_UINT>(a, blocks, stream);
     }
 }

@@ -11,6 +11,7 @@ in the reference.
 from __future__ import annotations
 
 import ctypes
+import enum
 from dataclasses import dataclass
 from typing import Optional, Tuple
 
@@ -354,3 +355,118 @@ def single_tile_items(key_dtype: torch.dtype, value_bytes: int = 0) -> int:
 def selector_flips(key_dtype: torch.dtype, value_bytes: int, n: int, bit_range: range) -> int:
     return _lib.lib().rsort_selector_flips(key_code(key_dtype), value_bytes, n,
                                            bit_range.start, bit_range.stop)
+
+
+# ---------------------------------------------------------------------------
+# DeviceMergeSort / DeviceMerge for named orders
+# ---------------------------------------------------------------------------
+class Order(enum.IntEnum):
+    """The comparators rccl-cub's merge sort is almost always given
+    (its `order: F` closure, dispatch.rs:170-175), by name:
+      ASCENDING         |a, b| a.cmp(b); floats partial_cmp, -0.0 == +0.0
+      DESCENDING        |a, b| b.cmp(a)
+      TOTAL_ASCENDING   |a, b| a.total_cmp(b): -0.0 < +0.0, NaNs by sign/payload
+      TOTAL_DESCENDING  |a, b| b.total_cmp(a)
+    A closure itself is device code and cannot cross the C ABI."""
+    ASCENDING = 0
+    DESCENDING = 1
+    TOTAL_ASCENDING = 2
+    TOTAL_DESCENDING = 3
+
+
+def order_code(order) -> int:
+    if isinstance(order, Order):
+        return int(order)
+    if isinstance(order, str):
+        try:
+            return int(Order[order.upper()])
+        except KeyError:
+            pass
+    if callable(order):
+        raise NotImplementedError(
+            "a comparator closure is device code; pass one of rccl_b200.cub.Order "
+            "(ASCENDING, DESCENDING, TOTAL_ASCENDING, TOTAL_DESCENDING)")
+    raise BadArgument(f"unknown sort order {order!r}")
+
+
+def device_merge_sort_keys_workspace(launch: Launch, key_dtype: torch.dtype,
+                                     n: int) -> DeviceRadixSortKeysWorkspace:
+    """Workspace of device_merge_sort_keys (workspace.rs:253-267): scratch keys
+    and the radix controls (the named orders run on the radix path)."""
+    return device_radix_sort_workspace(launch, key_dtype, n)
+
+
+def device_merge_sort_pairs_workspace(launch: Launch, key_dtype: torch.dtype, value_dtype,
+                                      n: int) -> DeviceRadixSortPairsWorkspace:
+    """Workspace of device_merge_sort_pairs (workspace.rs:269-286)."""
+    return device_radix_sort_pairs_workspace(launch, key_dtype, value_dtype, n)
+
+
+def device_merge_sort_keys(launch: Launch, keys: torch.Tensor,
+                           workspace: DeviceRadixSortKeysWorkspace, order) -> None:
+    """Stable in-place sort by a named order (dispatch.rs:170-193)."""
+    code = order_code(order)
+    launch.check(keys, workspace.scratch_keys)
+    raise_for(_lib.lib().rsort_merge_sort_keys(
+        key_code(keys.dtype), code, keys.data_ptr(), workspace.scratch_keys.data_ptr(),
+        workspace.scratch_keys.numel(), keys.numel(), *workspace.controls.args(), launch.handle))
+
+
+def device_merge_sort_pairs(launch: Launch, keys: torch.Tensor, values: torch.Tensor,
+                            workspace: DeviceRadixSortPairsWorkspace, order) -> None:
+    """Stable in-place key/value sort by a named order (dispatch.rs:1113-1146)."""
+    code = order_code(order)
+    launch.check(keys, values, workspace.scratch_keys, workspace.scratch_values)
+    if values.shape[0] != keys.numel():
+        raise LengthMismatch("merge sort values", keys.numel(), values.shape[0])
+    vb = value_bytes_of(values)
+    if value_bytes_of(workspace.scratch_values) != vb:
+        raise BadArgument("scratch values width differs from values")
+    raise_for(_lib.lib().rsort_merge_sort_pairs(
+        key_code(keys.dtype), code, keys.data_ptr(), values.data_ptr(), vb,
+        workspace.scratch_keys.data_ptr(), workspace.scratch_keys.numel(),
+        workspace.scratch_values.data_ptr(), workspace.scratch_values.shape[0], keys.numel(),
+        *workspace.controls.args(), launch.handle))
+
+
+@dataclass
+class DeviceMergeWorkspace:
+    """Merge-path partitions of a two-run merge (workspace.rs:223-233, 413-420)."""
+    partitions: torch.Tensor
+
+
+def device_merge_workspace(launch: Launch, first_len: int, second_len: int) -> DeviceMergeWorkspace:
+    words = _lib.lib().rsort_merge_partition_words(first_len + second_len)
+    return DeviceMergeWorkspace(torch.zeros(max(words, 1), dtype=torch.int64, device=launch.device))
+
+
+def _merge(launch, fk, fv, sk, sv, ws, ok, ov, order) -> None:
+    code = order_code(order)
+    launch.check(fk, sk, ok, fv, sv, ov)
+    if fk.dtype != sk.dtype or ok.dtype != fk.dtype:
+        raise BadArgument("merge inputs and output differ in key type")
+    na, nb = fk.numel(), sk.numel()
+    if ok.numel() != na + nb:
+        raise LengthMismatch("merge output", na + nb, ok.numel())
+    vb = 0
+    if fv is not None:
+        vb = value_bytes_of(fv)
+        if fv.shape[0] != na or sv.shape[0] != nb or ov.shape[0] != na + nb:
+            raise LengthMismatch("merge values", na + nb, ov.shape[0])
+    raise_for(_lib.lib().rsort_merge_ordered(
+        key_code(fk.dtype), code, fk.data_ptr() if na else None, _ptr(fv) if na else None, na,
+        sk.data_ptr() if nb else None, _ptr(sv) if nb else None, nb, ok.data_ptr(), _ptr(ov), vb,
+        ws.partitions.data_ptr(), ws.partitions.numel(), launch.handle))
+
+
+def device_merge_keys(launch: Launch, first: torch.Tensor, second: torch.Tensor,
+                      workspace: DeviceMergeWorkspace, output: torch.Tensor, order) -> None:
+    """Merge two sorted key ranges; ties take `first` (dispatch.rs:1570-1601)."""
+    _merge(launch, first, None, second, None, workspace, output, None, order)
+
+
+def device_merge_pairs(launch: Launch, first_keys, first_values, second_keys, second_values,
+                       workspace: DeviceMergeWorkspace, output_keys, output_values, order) -> None:
+    """Merge two sorted key/value ranges (dispatch.rs:1913-1960)."""
+    _merge(launch, first_keys, first_values, second_keys, second_values, workspace, output_keys,
+           output_values, order)

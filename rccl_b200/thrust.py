@@ -6,7 +6,8 @@ rccl-thrust/src/backend.rs:8-110: one temporary byte block split into aligned
 regions (scratch keys[, scratch values], bins, lookback, counters), the CUB
 sort, release of the block, then a stream synchronization.  The comparator
 forms `sort_by` / `sort_unstable_by` lower to DeviceMergeSort in the reference
-(backend.rs:39-63, 112-150), which this package does not provide.
+(backend.rs:39-63, 112-150); here they take a named order (rccl_b200.cub.Order:
+the comparator closure itself is device code) and give the stable sort by it.
 """
 from __future__ import annotations
 
@@ -15,8 +16,8 @@ from typing import Optional
 import torch
 
 from . import _lib
-from .cub import (KEY_TYPES, BadArgument, ContextMismatch, Launch, Program as CubProgram,
-                  controls_counts, key_code, value_bytes_of)
+from .cub import (KEY_TYPES, BadArgument, ContextMismatch, Launch, Order, Program as CubProgram,
+                  controls_counts, key_code, order_code, value_bytes_of)
 from .errors import LengthMismatch, raise_for
 
 
@@ -77,7 +78,9 @@ class _Temporary:
                 self.block[self.offsets[i]:self.offsets[i] + nbytes].zero_()
 
 
-def _radix_sort(execution: Execution, keys: torch.Tensor) -> None:
+def _radix_sort(execution: Execution, keys: torch.Tensor, order: Optional[int] = None) -> None:
+    """order: None for the radix lowering, else a named-order code for the
+    sort_by lowering (the same temporaries and the same synchronization)."""
     launch = execution.launch
     launch.check(keys)
     code = key_code(keys.dtype)
@@ -87,8 +90,13 @@ def _radix_sort(execution: Execution, keys: torch.Tensor) -> None:
     # alignments 128, 256, 256, 256.
     tmp = _Temporary(launch.device, [n * kb, nb * 8, nl * 4, nc * 4], [128, 256, 256, 256])
     tmp.zero(3, nc * 4, launch.stream)
-    st = _lib.lib().rsort_keys(code, 0, keys.data_ptr(), tmp.ptr(0), n, n, tmp.ptr(1), nb,
-                               tmp.ptr(2), nl, tmp.ptr(3), nc, launch.handle)
+    if order is None:
+        st = _lib.lib().rsort_keys(code, 0, keys.data_ptr(), tmp.ptr(0), n, n, tmp.ptr(1), nb,
+                                   tmp.ptr(2), nl, tmp.ptr(3), nc, launch.handle)
+    else:
+        st = _lib.lib().rsort_merge_sort_keys(code, order, keys.data_ptr(), tmp.ptr(0), n, n,
+                                              tmp.ptr(1), nb, tmp.ptr(2), nl, tmp.ptr(3), nc,
+                                              launch.handle)
     raise_for(st)
     # backend.rs:33-36: release the block (stream-ordered by the caching
     # allocator), then synchronize.
@@ -98,7 +106,8 @@ def _radix_sort(execution: Execution, keys: torch.Tensor) -> None:
     raise_for(status)
 
 
-def _radix_sort_pairs(execution: Execution, keys: torch.Tensor, values: torch.Tensor) -> None:
+def _radix_sort_pairs(execution: Execution, keys: torch.Tensor, values: torch.Tensor,
+                      order: Optional[int] = None) -> None:
     launch = execution.launch
     launch.check(keys, values)
     code = key_code(keys.dtype)
@@ -112,9 +121,14 @@ def _radix_sort_pairs(execution: Execution, keys: torch.Tensor, values: torch.Te
     tmp = _Temporary(launch.device, [n * kb, n * vb, nb * 8, nl * 4, nc * 4],
                      [128, 128, 256, 256, 256])
     tmp.zero(4, nc * 4, launch.stream)
-    st = _lib.lib().rsort_pairs(code, 0, keys.data_ptr(), values.data_ptr(), vb, tmp.ptr(0), n,
-                                tmp.ptr(1), n, n, tmp.ptr(2), nb, tmp.ptr(3), nl, tmp.ptr(4), nc,
-                                launch.handle)
+    if order is None:
+        st = _lib.lib().rsort_pairs(code, 0, keys.data_ptr(), values.data_ptr(), vb, tmp.ptr(0),
+                                    n, tmp.ptr(1), n, n, tmp.ptr(2), nb, tmp.ptr(3), nl,
+                                    tmp.ptr(4), nc, launch.handle)
+    else:
+        st = _lib.lib().rsort_merge_sort_pairs(code, order, keys.data_ptr(), values.data_ptr(),
+                                               vb, tmp.ptr(0), n, tmp.ptr(1), n, n, tmp.ptr(2),
+                                               nb, tmp.ptr(3), nl, tmp.ptr(4), nc, launch.handle)
     raise_for(st)
     status = _lib.lib().rsort_check_device_status(tmp.ptr(4) if nc else None, nc, launch.handle)
     del tmp
@@ -133,11 +147,15 @@ def sort_unstable(execution: Execution, keys: torch.Tensor) -> None:
 
 
 def sort_by(execution: Execution, keys: torch.Tensor, order) -> None:
-    raise NotImplementedError("comparator sorts lower to DeviceMergeSort, which rccl_b200 "
-                              "does not provide")
+    """Stable in-place sort by a named order (DeviceSortExt::sort_by,
+    ordering.rs:78-87; the reference lowers it to DeviceMergeSort).  `order`
+    is a rccl_b200.cub.Order: the comparator closure itself is device code."""
+    _radix_sort(execution, keys, order_code(order))
 
 
-sort_unstable_by = sort_by
+def sort_unstable_by(execution: Execution, keys: torch.Tensor, order) -> None:
+    """DeviceSortExt::sort_unstable_by (ordering.rs:58-68); stable here."""
+    _radix_sort(execution, keys, order_code(order))
 
 
 class KeyValueRangeMut:
@@ -154,10 +172,11 @@ class KeyValueRangeMut:
         _radix_sort_pairs(execution, self.keys, self.values)
 
     def sort_by(self, execution: Execution, order) -> None:
-        raise NotImplementedError("comparator sorts lower to DeviceMergeSort, which rccl_b200 "
-                                  "does not provide")
+        """DeviceKeyValueSortExt::sort_by (ordering.rs:170-181) by a named order."""
+        _radix_sort_pairs(execution, self.keys, self.values, order_code(order))
 
-    sort_unstable_by = sort_by
+    def sort_unstable_by(self, execution: Execution, order) -> None:
+        _radix_sort_pairs(execution, self.keys, self.values, order_code(order))
 
 
 class RangeError(ValueError):
