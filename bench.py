@@ -400,8 +400,11 @@ def run_single(args, workload: Workload):
     kernel_ms = {k: {"launches": len(v), "total_ms": sum(v), "avg_ms": statistics.mean(v)}
                  for k, v in per_kernel.items()}
 
-    e2e = None if args.no_e2e else run_e2e(args, workload, keys_h, values_h, dev)
     del src_k, keys, src_v, values, ws
+    torch.cuda.empty_cache()
+    thrust_call = None if args.no_e2e else thrust_call_cost(args, workload, keys_h, values_h, dev,
+                                                             total_ms / args.steps)
+    e2e = None if args.no_e2e else run_e2e(args, workload, keys_h, values_h, dev)
     torch.cuda.empty_cache()
 
     value = workload.n * args.steps / (total_ms / 1e3)
@@ -410,12 +413,65 @@ def run_single(args, workload: Workload):
         "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": np.dtype(workload.key).name,
         "data": "synthetic (numpy PCG64, seeded)", "config": config_dict(args, workload),
-        "roofline": roofline, "e2e": e2e, "gpu_launches": launches,
+        "roofline": roofline, "e2e": e2e, "thrust_call": thrust_call, "gpu_launches": launches,
         "kernels": kernel_ms, "clocks": clocks.summary(), "output_checked": ok,
     }
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(workload)
     print(json.dumps(line), flush=True)
+
+
+def thrust_sort(execution, dk, dv, descending: bool) -> None:
+    """One call of the public Thrust-style API: sort() / with_values().sort(),
+    or sort_by(DESCENDING) for descending workloads (rccl-thrust's
+    comparator-free sort is ascending only)."""
+    from rccl_b200 import cub, thrust
+    if descending:
+        if dv is None:
+            thrust.sort_by(execution, dk, cub.Order.DESCENDING)
+        else:
+            thrust.with_values(dk, dv).sort_by(execution, cub.Order.DESCENDING)
+    elif dv is None:
+        thrust.sort(execution, dk)
+    else:
+        thrust.with_values(dk, dv).sort(execution)
+
+
+def thrust_api_name(workload: Workload, keys_only: bool) -> str:
+    name = {(True, True): "rccl_b200.thrust sort_by(Order.DESCENDING)",
+            (True, False): "rccl_b200.thrust with_values().sort_by(Order.DESCENDING)",
+            (False, True): "rccl_b200.thrust sort()",
+            (False, False): "rccl_b200.thrust with_values().sort()"}[(bool(workload.desc), keys_only)]
+    return name + " (temporary allocation + sync per call)"
+
+
+def thrust_call_cost(args, workload: Workload, keys_h, values_h, dev, device_ms: float):
+    """Host time of the synchronous Thrust-style call on device-resident data
+    (temporary allocation from the caching allocator, the sort, the stream
+    synchronization) beside the device-timed sort: the per-call cost the
+    reference's Thrust path adds."""
+    import torch
+    from rccl_b200 import thrust
+    execution = thrust.Program.load(dev).par()
+    src_k = torch.from_numpy(keys_h).to(dev)
+    src_v = torch.from_numpy(values_h).to(dev) if values_h is not None else None
+    dk = torch.empty_like(src_k)
+    dv = torch.empty_like(src_v) if src_v is not None else None
+    times = []
+    for i in range(2 + max(1, min(args.steps, 5))):
+        dk.copy_(src_k)
+        if dv is not None:
+            dv.copy_(src_v)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        thrust_sort(execution, dk, dv, workload.desc)
+        t1 = time.perf_counter()
+        if i >= 2:
+            times.append((t1 - t0) * 1e3)
+    ms = statistics.mean(times)
+    return {"ms": ms, "device_ms": device_ms, "overhead_ms": ms - device_ms,
+            "api": thrust_api_name(workload, values_h is None),
+            "timing": "host wall clock around the synchronous call, inputs resident"}
 
 
 def run_e2e(args, workload: Workload, keys_h, values_h, dev):
@@ -459,22 +515,7 @@ def run_e2e(args, workload: Workload, keys_h, values_h, dev):
         b = i % NB
         dk, dv = dks[b], dvs[b]
         stream.wait_event(uploaded[b])
-        if workload.desc:
-            # rccl-thrust has no comparator-free descending sort; use the CUB
-            # descending entry point through the same temporary-allocating path.
-            from rccl_b200 import cub
-            launch = execution.launch
-            if dv is None:
-                ws = cub.device_radix_sort_workspace(launch, dk.dtype, dk.numel())
-                cub.device_radix_sort_keys_descending(launch, dk, ws)
-            else:
-                ws = cub.device_radix_sort_pairs_workspace(launch, dk.dtype, dv.dtype, dk.numel())
-                cub.device_radix_sort_pairs_descending(launch, dk, dv, ws)
-            stream.synchronize()
-        elif dv is None:
-            thrust.sort(execution, dk)
-        else:
-            thrust.with_values(dk, dv).sort(execution)
+        thrust_sort(execution, dk, dv, workload.desc)
         sorted_[b].record(stream)
 
     def download(i):
@@ -512,12 +553,7 @@ def run_e2e(args, workload: Workload, keys_h, values_h, dev):
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": h2d, "steps": steps,
             "output_checked": ok,
             "pipelined": "step i+1's upload overlaps step i's sort and download",
-            "api": ({(True, True): "rccl_b200.cub device_radix_sort_keys_descending",
-                     (True, False): "rccl_b200.cub device_radix_sort_pairs_descending",
-                     (False, True): "rccl_b200.thrust sort()",
-                     (False, False): "rccl_b200.thrust with_values().sort()"}[
-                         (bool(workload.desc), values_h is None)]
-                    + " (temporary allocation + sync per call)")}
+            "api": thrust_api_name(workload, values_h is None)}
 
 
 def run_cub_proxy(args, workload: Workload):
