@@ -33,14 +33,26 @@ extern "C" {
 /* Same binary layout as cudaStream_t. */
 typedef struct CUstream_st *rsort_stream_t;
 
-/* The six RadixKey implementations (rccl-cub/src/radix.rs:114-173). */
+/* The six RadixKey implementations (rccl-cub/src/radix.rs:114-173), then the
+ * small keys the reference lists as missing (no reference counterpart):
+ * u8/i8/u16/i16, IEEE half (F16) and bfloat16 (BF16), ordered by the same
+ * rules (floats: -0.0 == +0.0 in the radix order, NaNs by bit pattern).  The
+ * small keys are accepted by the single-GPU sorts (rsort_keys*, rsort_pairs*,
+ * rsort_merge_sort_*) but not by the sample-sort steps, the merges or
+ * rsort_keys_static. */
 typedef enum {
     RSORT_U32 = 0,
     RSORT_I32 = 1,
     RSORT_F32 = 2,
     RSORT_U64 = 3,
     RSORT_I64 = 4,
-    RSORT_F64 = 5
+    RSORT_F64 = 5,
+    RSORT_U8 = 6,
+    RSORT_I8 = 7,
+    RSORT_U16 = 8,
+    RSORT_I16 = 9,
+    RSORT_F16 = 10,
+    RSORT_BF16 = 11
 } rsort_key_t;
 
 /* Maps 1:1 onto rccl_cub::DeviceAlgorithmError (rccl-cub/src/error.rs:3-25). */

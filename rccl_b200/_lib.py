@@ -14,6 +14,8 @@ LIB_PATH = os.path.join(LIB_DIR, "librsort_b200.so")
 
 # rsort_key_t
 RSORT_U32, RSORT_I32, RSORT_F32, RSORT_U64, RSORT_I64, RSORT_F64 = range(6)
+# small keys (no reference counterpart)
+RSORT_U8, RSORT_I8, RSORT_U16, RSORT_I16, RSORT_F16, RSORT_BF16 = range(6, 12)
 
 # rsort_status
 RSORT_OK = 0

@@ -82,17 +82,36 @@ rsort_status cuda_fail(cudaError_t e, const char *role) {
     return fail(RSORT_CUDA_ERROR, role);
 }
 
-bool key_ok(rsort_key_t k) { return int(k) >= RSORT_U32 && int(k) <= RSORT_F64; }
-int key_bytes(rsort_key_t k) { return int(k) >= RSORT_U64 ? 8 : 4; }
+bool key_ok(rsort_key_t k) { return int(k) >= RSORT_U32 && int(k) <= RSORT_BF16; }
+int key_bytes(rsort_key_t k) {
+    switch (k) {
+        case RSORT_U8:
+        case RSORT_I8: return 1;
+        case RSORT_U16:
+        case RSORT_I16:
+        case RSORT_F16:
+        case RSORT_BF16: return 2;
+        case RSORT_U64:
+        case RSORT_I64:
+        case RSORT_F64: return 8;
+        default: return 4;
+    }
+}
 int key_kind(rsort_key_t k) {
     switch (k) {
         case RSORT_I32:
-        case RSORT_I64: return KIND_SINT;
+        case RSORT_I64:
+        case RSORT_I8:
+        case RSORT_I16: return KIND_SINT;
         case RSORT_F32:
-        case RSORT_F64: return KIND_FLOAT;
+        case RSORT_F64:
+        case RSORT_F16:
+        case RSORT_BF16: return KIND_FLOAT;
         default: return KIND_UINT;
     }
 }
+// The sample-sort steps and the merges are built for 32- and 64-bit keys.
+bool wide_key(rsort_key_t k) { return key_ok(k) && key_bytes(k) >= 4; }
 bool value_ok(size_t vb) { return vb == 0 || vb == 1 || vb == 2 || vb == 4 || vb == 8 || vb == 16; }
 
 struct DeviceInfo {
@@ -488,7 +507,7 @@ void rsort_launch_count_reset(void) { g_launches = 0; }
 rsort_status rsort_dist_samples(rsort_key_t key, int descending, const void *d_sorted_keys,
                                 size_t m, unsigned rank, unsigned samples, void *d_samples,
                                 rsort_stream_t stream) {
-    if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
+    if (!wide_key(key)) return fail(RSORT_BAD_ARGUMENT, "key type (32- or 64-bit keys only)");
     if (m >= (size_t(1) << POS_BITS) || rank >= (1u << (64 - POS_BITS)))
         return fail(RSORT_SIZE_OVERFLOW, "sample position");
     if (samples == 0) return RSORT_OK;
@@ -530,7 +549,7 @@ rsort_status rsort_dist_splitters(const void *d_samples, size_t total, unsigned 
 rsort_status rsort_dist_bounds(rsort_key_t key, int descending, const void *d_sorted_keys,
                                size_t m, unsigned rank, const void *d_splitters, unsigned world,
                                uint64_t *d_bounds, rsort_stream_t stream) {
-    if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
+    if (!wide_key(key)) return fail(RSORT_BAD_ARGUMENT, "key type (32- or 64-bit keys only)");
     if (world < 1 || !d_bounds || (world > 1 && !d_splitters))
         return fail(RSORT_BAD_ARGUMENT, "null buffer");
     if (m >= (size_t(1) << POS_BITS)) return fail(RSORT_SIZE_OVERFLOW, "sample position");
@@ -645,7 +664,7 @@ rsort_status merge_impl(rsort_key_t key, int descending, bool total, const void 
                         const void *a_values, size_t na, const void *b_keys, const void *b_values,
                         size_t nb, void *out_keys, void *out_values, size_t value_bytes,
                         uint64_t *d_partitions, size_t npartitions, rsort_stream_t stream) {
-    if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
+    if (!wide_key(key)) return fail(RSORT_BAD_ARGUMENT, "key type (32- or 64-bit keys only)");
     if (!value_ok(value_bytes)) return fail(RSORT_BAD_ARGUMENT, "radix value width");
     if (na + nb == 0) return RSORT_OK;
     if (!out_keys || (na && !a_keys) || (nb && !b_keys) ||
@@ -675,7 +694,7 @@ rsort_status rsort_merge_runs(rsort_key_t key, int descending, void *keys, void 
                               size_t value_bytes, const size_t *run_lengths, unsigned runs,
                               void *scratch_keys, void *scratch_values, uint64_t *d_partitions,
                               size_t npartitions, int *result_in_scratch, rsort_stream_t stream) {
-    if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
+    if (!wide_key(key)) return fail(RSORT_BAD_ARGUMENT, "key type (32- or 64-bit keys only)");
     if (!value_ok(value_bytes)) return fail(RSORT_BAD_ARGUMENT, "radix value width");
     if (!result_in_scratch || (runs && !run_lengths)) return fail(RSORT_BAD_ARGUMENT, "null argument");
     const size_t kb = size_t(key_bytes(key));
@@ -735,7 +754,7 @@ rsort_status rsort_merge_segments(rsort_key_t key, int descending, unsigned runs
                                   uint64_t *d_partitions, size_t npartitions,
                                   int *result_in_scratch, unsigned first_pair,
                                   rsort_stream_t stream) {
-    if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
+    if (!wide_key(key)) return fail(RSORT_BAD_ARGUMENT, "key type (32- or 64-bit keys only)");
     if (!value_ok(value_bytes)) return fail(RSORT_BAD_ARGUMENT, "radix value width");
     if (!result_in_scratch || (runs && (!run_lengths || !run_keys || (value_bytes && !run_values))))
         return fail(RSORT_BAD_ARGUMENT, "null argument");

@@ -27,6 +27,16 @@ constexpr int DEV_STATUS_TIMEOUT = 7;
 constexpr int DEV_STATUS_BOUNDS = 8;
 
 template <typename B> struct KeyBits;
+template <> struct KeyBits<uint8_t> {
+    using Signed = int8_t;
+    static constexpr uint8_t SIGN = 0x80u;
+    static constexpr int WIDTH = 8;
+};
+template <> struct KeyBits<uint16_t> {
+    using Signed = int16_t;
+    static constexpr uint16_t SIGN = 0x8000u;
+    static constexpr int WIDTH = 16;
+};
 template <> struct KeyBits<uint32_t> {
     using Signed = int32_t;
     static constexpr uint32_t SIGN = 0x80000000u;
@@ -134,6 +144,16 @@ __device__ __forceinline__ uint32_t lanemask_gt() {
 }
 
 // Streaming (read-once) global loads: no L1 allocation.
+__device__ __forceinline__ uint8_t ld_stream(const uint8_t *p) {
+    uint16_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.u8 %0, [%1];" : "=h"(v) : "l"(p));
+    return uint8_t(v);
+}
+__device__ __forceinline__ uint16_t ld_stream(const uint16_t *p) {
+    uint16_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
+}
 __device__ __forceinline__ uint32_t ld_stream(const uint32_t *p) {
     uint32_t v;
     asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));

@@ -46,7 +46,7 @@ constexpr int HIST_UNROLL = 4;
 
 template <typename B> struct HistShape {
     static constexpr int MAX_PASSES = int(sizeof(B));  // 8-bit digits
-    static constexpr int COLS = sizeof(B) == 4 ? 32 : 16;
+    static constexpr int COLS = sizeof(B) <= 4 ? 32 : 16;
     static constexpr size_t WORDS = size_t(MAX_PASSES) * RADIX * COLS;
     static constexpr size_t BYTES = WORDS * 4;
 };
@@ -150,7 +150,15 @@ __global__ void __launch_bounds__(HIST_THREADS, 1) histogram_kernel(HistArgs a) 
 #pragma unroll
             for (int u = 0; u < HIST_UNROLL; ++u) {
                 if (i + uint64_t(u) * stride >= nvec) break;
-                if constexpr (sizeof(B) == 4) {
+                if constexpr (sizeof(B) == 1 || sizeof(B) == 2) {
+                    const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+#pragma unroll
+                        for (int b = 0; b < 4 / int(sizeof(B)); ++b)
+                            count(B(w[q] >> (8 * sizeof(B) * b)));
+                    }
+                } else if constexpr (sizeof(B) == 4) {
                     count(v[u].x);
                     count(v[u].y);
                     count(v[u].z);
@@ -752,20 +760,35 @@ static cudaError_t histogram_kind(const HistArgs &a, int blocks, cudaStream_t st
 cudaError_t launch_histogram(int key_bytes, const HistArgs &a, int sm_count, cudaStream_t stream) {
     // One 1024-thread CTA per SM (the counters fill the SM's shared memory).
     const int blocks = sm_count;
-    return key_bytes == 4 ? histogram_kind<uint32_t>(a, blocks, stream)
-                          : histogram_kind<uint64_t>(a, blocks, stream);
+    switch (key_bytes) {
+        case 1: return histogram_kind<uint8_t>(a, blocks, stream);
+        case 2: return histogram_kind<uint16_t>(a, blocks, stream);
+        case 4: return histogram_kind<uint32_t>(a, blocks, stream);
+        case 8: return histogram_kind<uint64_t>(a, blocks, stream);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 cudaError_t launch_onesweep(int key_bytes, int value_bytes, const PassArgs &a, uint64_t tiles,
                             cudaStream_t stream) {
-    return key_bytes == 4 ? onesweep_vb<uint32_t>(value_bytes, a, tiles, stream)
-                          : onesweep_vb<uint64_t>(value_bytes, a, tiles, stream);
+    switch (key_bytes) {
+        case 1: return onesweep_vb<uint8_t>(value_bytes, a, tiles, stream);
+        case 2: return onesweep_vb<uint16_t>(value_bytes, a, tiles, stream);
+        case 4: return onesweep_vb<uint32_t>(value_bytes, a, tiles, stream);
+        case 8: return onesweep_vb<uint64_t>(value_bytes, a, tiles, stream);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 cudaError_t launch_single_tile(int key_bytes, int value_bytes, const SingleArgs &a,
                                cudaStream_t stream) {
-    return key_bytes == 4 ? single_vb<uint32_t>(value_bytes, a, stream)
-                          : single_vb<uint64_t>(value_bytes, a, stream);
+    switch (key_bytes) {
+        case 1: return single_vb<uint8_t>(value_bytes, a, stream);
+        case 2: return single_vb<uint16_t>(value_bytes, a, stream);
+        case 4: return single_vb<uint32_t>(value_bytes, a, stream);
+        case 8: return single_vb<uint64_t>(value_bytes, a, stream);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 }  // namespace rsort

@@ -32,7 +32,10 @@ constexpr int ONESWEEP_THREADS = RSORT_ONESWEEP_THREADS;
 #ifndef RSORT_ITEMS_PAIRS32_32
 #define RSORT_ITEMS_PAIRS32_32 16
 #endif
-constexpr int onesweep_items(int key_bytes, int value_bytes) {
+// 1- and 2-byte keys take the 4-byte shapes (a key occupies one register
+// either way).
+constexpr int onesweep_items(int key_bytes_, int value_bytes) {
+    const int key_bytes = key_bytes_ < 4 ? 4 : key_bytes_;
     return (value_bytes == 0 && key_bytes == 4) ? RSORT_ITEMS_KEYS32
          : (value_bytes == 0 && key_bytes == 8) ? RSORT_ITEMS_KEYS64
          : (value_bytes == 4 && key_bytes == 8) ? RSORT_ITEMS_PAIRS64_32

@@ -28,7 +28,18 @@ KEY_TYPES = {
     torch.int64: _lib.RSORT_I64,
     torch.float64: _lib.RSORT_F64,
 }
-KEY_BITS = {k: (32 if v < _lib.RSORT_U64 else 64) for k, v in KEY_TYPES.items()}
+# Small keys (no reference counterpart; the reference lists them as missing):
+# accepted by the single-GPU radix and named-order sorts.
+SMALL_KEY_TYPES = {
+    torch.uint8: _lib.RSORT_U8,
+    torch.int8: _lib.RSORT_I8,
+    torch.uint16: _lib.RSORT_U16,
+    torch.int16: _lib.RSORT_I16,
+    torch.float16: _lib.RSORT_F16,
+    torch.bfloat16: _lib.RSORT_BF16,
+}
+KEY_BITS = {k: torch.empty(0, dtype=k).element_size() * 8
+            for k in list(KEY_TYPES) + list(SMALL_KEY_TYPES)}
 
 
 class ContextMismatch(DeviceAlgorithmError):
@@ -37,9 +48,10 @@ class ContextMismatch(DeviceAlgorithmError):
 
 def key_code(dtype: torch.dtype) -> int:
     try:
-        return KEY_TYPES[dtype]
+        return KEY_TYPES[dtype] if dtype in KEY_TYPES else SMALL_KEY_TYPES[dtype]
     except KeyError:
-        raise BadArgument(f"{dtype} is not a RadixKey (u32/i32/f32/u64/i64/f64)") from None
+        raise BadArgument(f"{dtype} is not a RadixKey (u32/i32/f32/u64/i64/f64, or "
+                          "u8/i8/u16/i16/f16/bf16)") from None
 
 
 def value_bytes_of(t: torch.Tensor) -> int:
