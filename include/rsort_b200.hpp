@@ -30,6 +30,12 @@ template <> struct RadixKey<float> { static constexpr rsort_key_t code = RSORT_F
 template <> struct RadixKey<uint64_t> { static constexpr rsort_key_t code = RSORT_U64; };
 template <> struct RadixKey<int64_t> { static constexpr rsort_key_t code = RSORT_I64; };
 template <> struct RadixKey<double> { static constexpr rsort_key_t code = RSORT_F64; };
+// Small integer keys (no reference counterpart).  Half and bfloat16 keys go
+// through the C ABI with RSORT_F16 / RSORT_BF16 on their 16-bit storage.
+template <> struct RadixKey<uint8_t> { static constexpr rsort_key_t code = RSORT_U8; };
+template <> struct RadixKey<int8_t> { static constexpr rsort_key_t code = RSORT_I8; };
+template <> struct RadixKey<uint16_t> { static constexpr rsort_key_t code = RSORT_U16; };
+template <> struct RadixKey<int16_t> { static constexpr rsort_key_t code = RSORT_I16; };
 
 // DeviceAlgorithmError: one exception type whose `kind` names the variant and
 // whose fields carry that variant's payload.
