@@ -267,6 +267,22 @@ rsort_status rsort_merge_ordered(rsort_key_t key, rsort_order_t order, const voi
                                  size_t npartitions, rsort_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Lexicographic record sort (rccl-thrust/src/record_sort.rs:144-300).
+ *
+ * Stable ascending sort of n padding-free rows of `words` uint32 each (word 0
+ * most significant; SRDatalog/HISA records), in place.  An optional payload
+ * of payload_bytes per row (0 = none) moves in lockstep; equal rows keep
+ * their input order.  Multi-word LSD over the stable pairs radix sort: one
+ * pass per 64-bit chunk of the row, then one gather of rows and payloads.
+ * d_scratch: rsort_rows_scratch_bytes(words, payload_bytes, n) bytes, 256-byte
+ * aligned.  n must fit a 32-bit permutation.
+ * ------------------------------------------------------------------------- */
+size_t rsort_rows_scratch_bytes(size_t words, size_t payload_bytes, size_t n);
+rsort_status rsort_rows_lexicographic(size_t words, void *d_rows, void *d_payload,
+                                      size_t payload_bytes, size_t n, void *d_scratch,
+                                      size_t scratch_bytes, rsort_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Bucket exchange over NVLink peer memory (no reference counterpart).
  *
  * Replaces step 5 above (the NCCL all-to-all): every rank exports its sorted
@@ -329,7 +345,7 @@ void rsort_launch_count_reset(void);
 /* Kernel ids reported by rsort_profile_read. */
 enum { RSORT_KERNEL_INIT = 0, RSORT_KERNEL_HISTOGRAM = 1, RSORT_KERNEL_ONESWEEP = 2,
        RSORT_KERNEL_SINGLE_TILE = 3, RSORT_KERNEL_DIST = 4, RSORT_KERNEL_MERGE = 5,
-       RSORT_KERNEL_GATHER = 6 };
+       RSORT_KERNEL_GATHER = 6, RSORT_KERNEL_RECORDS = 7 };
 
 /* Benchmark instrumentation (no reference counterpart): while enabled, every
  * kernel launch of the calling host thread is bracketed by CUDA events on its

@@ -30,7 +30,7 @@ RSORT_BAD_ARGUMENT = 8
 
 # kernel ids of rsort_profile_read
 KERNEL_NAMES = {0: "init", 1: "histogram", 2: "onesweep", 3: "single_tile", 4: "dist",
-                5: "merge", 6: "gather"}
+                5: "merge", 6: "gather", 7: "records"}
 IPC_HANDLE_BYTES = 64
 GATHER_MAX_SEGMENTS = 64
 
@@ -65,6 +65,8 @@ EXPORTED_SYMBOLS = (
     "rsort_merge_sort_keys",
     "rsort_merge_sort_pairs",
     "rsort_merge_ordered",
+    "rsort_rows_scratch_bytes",
+    "rsort_rows_lexicographic",
 )
 
 
@@ -153,6 +155,10 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.rsort_merge_sort_pairs.restype = i
     lib.rsort_merge_ordered.argtypes = [i, i, vp, vp, sz, vp, vp, sz, vp, vp, sz, vp, sz, vp]
     lib.rsort_merge_ordered.restype = i
+    lib.rsort_rows_scratch_bytes.argtypes = [sz, sz, sz]
+    lib.rsort_rows_scratch_bytes.restype = sz
+    lib.rsort_rows_lexicographic.argtypes = [sz, vp, vp, sz, sz, vp, sz, vp]
+    lib.rsort_rows_lexicographic.restype = i
 
 
 def lib() -> ctypes.CDLL:

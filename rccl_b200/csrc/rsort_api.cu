@@ -10,6 +10,7 @@
 #include "rsort_device.cuh"
 #include "rsort_dist.cuh"
 #include "rsort_kernels.cuh"
+#include "rsort_records.cuh"
 
 using namespace rsort;
 
@@ -629,6 +630,121 @@ rsort_status rsort_gather_segments(unsigned nseg, const void *const *d_src, cons
         e = launch_gather(a, dev.sm_count, s);
     }
     return e == cudaSuccess ? RSORT_OK : cuda_fail(e, "gather launch");
+}
+
+// ---------------------------------------------------------------------------
+// Lexicographic record sort (rccl-thrust/src/record_sort.rs:144-300)
+// ---------------------------------------------------------------------------
+namespace {
+
+struct RowsLayout {
+    size_t keys, keys_alt, perm, perm_alt, bins, lookback, counters, rows, payload, total;
+    rsort_controls c;
+};
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+rsort_status rows_layout(size_t words, size_t payload_bytes, size_t n, RowsLayout *L) {
+    rsort_controls c{};
+    rsort_status st = rsort_controls_query(RSORT_U64, 4, n, &c);
+    if (st != RSORT_OK) return st;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = off;
+        off = align256(off + bytes);
+        return at;
+    };
+    L->keys = take(8 * n);
+    L->keys_alt = take(8 * n);
+    L->perm = take(4 * n);
+    L->perm_alt = take(4 * n);
+    L->bins = take(8 * c.bins);
+    L->lookback = take(4 * c.lookback);
+    L->counters = take(4 * c.counters);
+    L->rows = take(4 * words * n);
+    L->payload = take(payload_bytes * n);
+    L->total = off;
+    L->c = c;
+    return RSORT_OK;
+}
+
+}  // namespace
+
+size_t rsort_rows_scratch_bytes(size_t words, size_t payload_bytes, size_t n) {
+    RowsLayout L{};
+    return rows_layout(words, payload_bytes, n, &L) == RSORT_OK ? L.total : 0;
+}
+
+rsort_status rsort_rows_lexicographic(size_t words, void *d_rows, void *d_payload,
+                                      size_t payload_bytes, size_t n, void *d_scratch,
+                                      size_t scratch_bytes, rsort_stream_t stream) {
+    if (words == 0 || n <= 1) return RSORT_OK;
+    if (n > 0xffffffffull) return fail(RSORT_SIZE_OVERFLOW, "record count (32-bit permutation)");
+    if (words > (size_t(1) << 20)) return fail(RSORT_BAD_ARGUMENT, "record width");
+    if (!d_rows || (payload_bytes && !d_payload)) return fail(RSORT_BAD_ARGUMENT, "null buffer");
+    RowsLayout L{};
+    rsort_status st = rows_layout(words, payload_bytes, n, &L);
+    if (st != RSORT_OK) return st;
+    if (!d_scratch || scratch_bytes < L.total)
+        return fail(RSORT_WORKSPACE_TOO_SMALL, "record sort scratch", L.total, scratch_bytes);
+    DeviceInfo dev;
+    st = device_info(&dev);
+    if (st != RSORT_OK) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    char *base = static_cast<char *>(d_scratch);
+    uint64_t *keys = reinterpret_cast<uint64_t *>(base + L.keys);
+    uint64_t *keys_alt = reinterpret_cast<uint64_t *>(base + L.keys_alt);
+    uint32_t *perm = reinterpret_cast<uint32_t *>(base + L.perm);
+    uint32_t *perm_alt = reinterpret_cast<uint32_t *>(base + L.perm_alt);
+    Controls c{reinterpret_cast<uint64_t *>(base + L.bins), L.c.bins,
+               reinterpret_cast<int32_t *>(base + L.lookback), L.c.lookback,
+               reinterpret_cast<int32_t *>(base + L.counters), L.c.counters};
+    const uint32_t *rows = static_cast<const uint32_t *>(d_rows);
+    cudaError_t e = L.c.counters ? cudaMemsetAsync(c.counters, 0, 4 * L.c.counters, s) : cudaSuccess;
+    if (e != cudaSuccess) return cuda_fail(e, "record sort counters");
+    {
+        LaunchScope scope(RSORT_KERNEL_RECORDS, s);
+        e = launch_iota(perm, n, dev.sm_count, s);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "record sort permutation");
+    // LSD over 64-bit chunks of the row, least significant chunk (the last
+    // words) first; every pass is a stable sort of (chunk key, permutation).
+    const size_t chunks = (words + 1) / 2;
+    for (size_t j = chunks; j-- > 0;) {
+        const uint32_t first = uint32_t(2 * j);
+        const uint32_t count = uint32_t(words - 2 * j < 2 ? words - 2 * j : 2);
+        {
+            LaunchScope scope(RSORT_KERNEL_RECORDS, s);
+            e = launch_chunk_keys(rows, uint32_t(words), j + 1 == chunks ? nullptr : perm, n, first,
+                                  count, keys, dev.sm_count, s);
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "record sort chunk keys");
+        int cur_first = 1;
+        st = sort_buffer(RSORT_U64, 0, keys, keys_alt, perm, perm_alt, 4, n, 0, 32 * count,
+                         &cur_first, c, s);
+        if (st != RSORT_OK) return st;
+        if (!cur_first) {
+            e = cudaMemcpyAsync(perm, perm_alt, 4 * n, cudaMemcpyDeviceToDevice, s);
+            if (e != cudaSuccess) return cuda_fail(e, "record sort permutation copy");
+        }
+    }
+    // Apply the permutation to the rows and payloads.
+    char *rows_tmp = base + L.rows;
+    {
+        LaunchScope scope(RSORT_KERNEL_RECORDS, s);
+        e = launch_permute(d_rows, perm, n, 4 * words, rows_tmp, dev.sm_count, s);
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d_rows, rows_tmp, 4 * words * n, cudaMemcpyDeviceToDevice, s);
+    if (e == cudaSuccess && payload_bytes) {
+        char *pay_tmp = base + L.payload;
+        {
+            LaunchScope scope(RSORT_KERNEL_RECORDS, s);
+            e = launch_permute(d_payload, perm, n, payload_bytes, pay_tmp, dev.sm_count, s);
+        }
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(d_payload, pay_tmp, payload_bytes * n, cudaMemcpyDeviceToDevice, s);
+    }
+    return e == cudaSuccess ? RSORT_OK : cuda_fail(e, "record sort permutation");
 }
 
 size_t rsort_merge_partition_words(size_t total) { return merge_partition_words(total, 0); }

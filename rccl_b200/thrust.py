@@ -18,7 +18,7 @@ import torch
 from . import _lib
 from .cub import (KEY_TYPES, BadArgument, ContextMismatch, Launch, Order, Program as CubProgram,
                   controls_counts, key_code, order_code, value_bytes_of)
-from .errors import LengthMismatch, raise_for
+from .errors import LengthMismatch, UnsupportedTarget, raise_for
 
 
 def _align(x: int, a: int) -> int:
@@ -190,3 +190,77 @@ def with_values(keys: torch.Tensor, values: torch.Tensor) -> KeyValueRangeMut:
     if keys.numel() != values.shape[0]:
         raise RangeError(keys.numel(), values.shape[0])
     return KeyValueRangeMut(keys, values)
+
+
+# ---------------------------------------------------------------------------
+# Lexicographic record sort (rccl-thrust/src/record_sort.rs:144-300)
+# ---------------------------------------------------------------------------
+_ROW_PAYLOADS = (torch.uint64, torch.int64, torch.float64, torch.bool, torch.uint8)
+
+
+def _sort_rows(execution: Execution, rows: torch.Tensor,
+               payload: Optional[torch.Tensor]) -> None:
+    """Stable ascending lexicographic sort of (n, N) uint32 rows in place,
+    payload rows in lockstep: multi-word LSD radix (rsort_rows_lexicographic)
+    with a temporary block, then a stream synchronization."""
+    launch = execution.launch
+    launch.check(rows, payload)
+    if rows.dim() != 2 or rows.dtype not in (torch.uint32, torch.int32):
+        raise BadArgument("rows must be an (n, N) uint32 tensor")
+    n, arity = rows.shape
+    # record_sort.rs:118-126
+    if not 2 <= arity <= 6:
+        raise UnsupportedTarget("record sort supports audited workload arities 2 through 6; "
+                                "use radix sort for scalar keys")
+    pb = 0
+    if payload is not None:
+        # record_sort.rs:128-141 and the sealed payload set (:24-31)
+        if payload.shape[0] != n:
+            raise LengthMismatch("record payloads", n, payload.shape[0])
+        if payload.dtype not in _ROW_PAYLOADS or payload.dim() != 1:
+            raise BadArgument("payloads: u64, f64 or Boolean provenance, one per row")
+        pb = payload.element_size()
+    lib = _lib.lib()
+    nbytes = lib.rsort_rows_scratch_bytes(arity, pb, n)
+    tmp = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=launch.device)
+    st = lib.rsort_rows_lexicographic(arity, rows.data_ptr(),
+                                      None if payload is None else payload.data_ptr(), pb, n,
+                                      tmp.data_ptr(), nbytes, launch.handle)
+    raise_for(st)
+    del tmp
+    execution.synchronize()
+
+
+def sort_rows_lexicographic(execution: Execution, rows: torch.Tensor) -> None:
+    """record_sort.rs:176-184"""
+    _sort_rows(execution, rows, None)
+
+
+def sort_rows_lexicographic_into(execution: Execution, input: torch.Tensor,
+                                 output: torch.Tensor) -> None:
+    """Stable out-of-place row sort (record_sort.rs:186-221)."""
+    if output.shape != input.shape:
+        raise LengthMismatch("record output", input.shape[0], output.shape[0])
+    with torch.cuda.stream(execution.stream):
+        output.copy_(input)
+    _sort_rows(execution, output, None)
+
+
+def sort_rows_with_payload_lexicographic(execution: Execution, rows: torch.Tensor,
+                                         payloads: torch.Tensor) -> None:
+    """record_sort.rs:223-271"""
+    _sort_rows(execution, rows, payloads)
+
+
+def sort_rows_with_payload_lexicographic_into(execution: Execution, rows: torch.Tensor,
+                                              payloads: torch.Tensor, rows_out: torch.Tensor,
+                                              payloads_out: torch.Tensor) -> None:
+    """Stable out-of-place row/payload sort (record_sort.rs:273-300)."""
+    if rows_out.shape != rows.shape:
+        raise LengthMismatch("record output", rows.shape[0], rows_out.shape[0])
+    if payloads_out.shape != payloads.shape:
+        raise LengthMismatch("record payload output", payloads.shape[0], payloads_out.shape[0])
+    with torch.cuda.stream(execution.stream):
+        rows_out.copy_(rows)
+        payloads_out.copy_(payloads)
+    _sort_rows(execution, rows_out, payloads_out)
