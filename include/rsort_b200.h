@@ -267,6 +267,26 @@ rsort_status rsort_merge_ordered(rsort_key_t key, rsort_order_t order, const voi
                                  size_t npartitions, rsort_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Segmented radix sort (no reference counterpart; the reference lists it as
+ * missing).  Sorts each segment [d_begin_offsets[i], d_end_offsets[i]) of
+ * the input (uint64 device arrays) into the same items of the output, stably,
+ * by bits [begin_bit, end_bit), exactly as rsort_keys_buffer / _pairs_buffer
+ * would sort an array of that segment's length.  Segments must not overlap;
+ * items outside every segment are left as they are in the output.
+ * Segments up to the single-tile extent are sorted one CTA each in one
+ * launch, longer ones by the onesweep path one after another.  The call reads
+ * the offsets on the host (it synchronizes the stream).  value_bytes 0 =
+ * keys only.  d_scratch: rsort_segmented_scratch_bytes(..) bytes.
+ * ------------------------------------------------------------------------- */
+size_t rsort_segmented_scratch_bytes(rsort_key_t key, size_t value_bytes, size_t n, size_t nseg);
+rsort_status rsort_segmented_sort(rsort_key_t key, int descending, const void *d_keys_in,
+                                  void *d_keys_out, const void *d_values_in, void *d_values_out,
+                                  size_t value_bytes, size_t n, size_t nseg,
+                                  const uint64_t *d_begin_offsets, const uint64_t *d_end_offsets,
+                                  unsigned begin_bit, unsigned end_bit, void *d_scratch,
+                                  size_t scratch_bytes, rsort_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Lexicographic record sort (rccl-thrust/src/record_sort.rs:144-300).
  *
  * Stable ascending sort of n padding-free rows of `words` uint32 each (word 0

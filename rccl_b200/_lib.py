@@ -67,6 +67,8 @@ EXPORTED_SYMBOLS = (
     "rsort_merge_ordered",
     "rsort_rows_scratch_bytes",
     "rsort_rows_lexicographic",
+    "rsort_segmented_scratch_bytes",
+    "rsort_segmented_sort",
 )
 
 
@@ -159,6 +161,11 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.rsort_rows_scratch_bytes.restype = sz
     lib.rsort_rows_lexicographic.argtypes = [sz, vp, vp, sz, sz, vp, sz, vp]
     lib.rsort_rows_lexicographic.restype = i
+    lib.rsort_segmented_scratch_bytes.argtypes = [i, sz, sz, sz]
+    lib.rsort_segmented_scratch_bytes.restype = sz
+    lib.rsort_segmented_sort.argtypes = [i, i, vp, vp, vp, vp, sz, sz, sz, vp, vp, u, u, vp, sz,
+                                         vp]
+    lib.rsort_segmented_sort.restype = i
 
 
 def lib() -> ctypes.CDLL:

@@ -633,6 +633,151 @@ rsort_status rsort_gather_segments(unsigned nseg, const void *const *d_src, cons
 }
 
 // ---------------------------------------------------------------------------
+// Segmented radix sort (no reference counterpart)
+// ---------------------------------------------------------------------------
+namespace {
+
+struct SegLayout {
+    size_t keys, values, bins, lookback, counters, ids, total;
+    rsort_controls c;
+};
+
+rsort_status seg_layout(rsort_key_t key, size_t vb, size_t n, size_t nseg, SegLayout *L) {
+    if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
+    rsort_controls c{};
+    // Controls sized for a segment of all n items bound every segment.
+    rsort_status st = rsort_controls_query(key, vb, n, &c);
+    if (st != RSORT_OK) return st;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = off;
+        off = (off + bytes + 255) / 256 * 256;
+        return at;
+    };
+    L->keys = take(size_t(key_bytes(key)) * n);
+    L->values = take(vb * n);
+    L->bins = take(8 * c.bins);
+    L->lookback = take(4 * c.lookback);
+    L->counters = take(4 * c.counters);
+    L->ids = take(4 * nseg);
+    L->total = off;
+    L->c = c;
+    return RSORT_OK;
+}
+
+}  // namespace
+
+size_t rsort_segmented_scratch_bytes(rsort_key_t key, size_t value_bytes, size_t n, size_t nseg) {
+    SegLayout L{};
+    return seg_layout(key, value_bytes, n, nseg, &L) == RSORT_OK ? L.total : 0;
+}
+
+rsort_status rsort_segmented_sort(rsort_key_t key, int descending, const void *d_keys_in,
+                                  void *d_keys_out, const void *d_values_in, void *d_values_out,
+                                  size_t value_bytes, size_t n, size_t nseg,
+                                  const uint64_t *d_begin_offsets, const uint64_t *d_end_offsets,
+                                  unsigned begin_bit, unsigned end_bit, void *d_scratch,
+                                  size_t scratch_bytes, rsort_stream_t stream) {
+    if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
+    if (!value_ok(value_bytes)) return fail(RSORT_BAD_ARGUMENT, "radix value width");
+    const int kb = key_bytes(key);
+    const unsigned kbits = unsigned(kb) * 8;
+    if (begin_bit > end_bit || end_bit > kbits) return fail_bits(begin_bit, end_bit, kbits);
+    if (nseg == 0 || n == 0) return RSORT_OK;
+    if (nseg > 0xffffffffull) return fail(RSORT_SIZE_OVERFLOW, "segment count");
+    if (!d_keys_in || !d_keys_out || !d_begin_offsets || !d_end_offsets ||
+        (value_bytes && (!d_values_in || !d_values_out)))
+        return fail(RSORT_BAD_ARGUMENT, "null buffer");
+    SegLayout L{};
+    rsort_status st = seg_layout(key, value_bytes, n, nseg, &L);
+    if (st != RSORT_OK) return st;
+    if (!d_scratch || scratch_bytes < L.total)
+        return fail(RSORT_WORKSPACE_TOO_SMALL, "segmented sort scratch", L.total, scratch_bytes);
+    DeviceInfo dev;
+    st = device_info(&dev);
+    if (st != RSORT_OK) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    // The segment extents are read on the host (one synchronization).
+    std::vector<uint64_t> b(nseg), e(nseg);
+    cudaError_t ce = cudaMemcpyAsync(b.data(), d_begin_offsets, 8 * nseg, cudaMemcpyDeviceToHost, s);
+    if (ce == cudaSuccess)
+        ce = cudaMemcpyAsync(e.data(), d_end_offsets, 8 * nseg, cudaMemcpyDeviceToHost, s);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(s);
+    if (ce != cudaSuccess) return cuda_fail(ce, "segment offsets");
+    const size_t single = policy800_single_tile_items(kb, int(value_bytes));
+    std::vector<uint32_t> small;
+    std::vector<size_t> large;
+    for (size_t i = 0; i < nseg; ++i) {
+        if (b[i] > e[i] || e[i] > n) return fail(RSORT_BAD_ARGUMENT, "segment offsets out of range");
+        const uint64_t len = e[i] - b[i];
+        if (len == 0) continue;
+        if (len <= single) small.push_back(uint32_t(i));
+        else large.push_back(i);
+    }
+    char *base = static_cast<char *>(d_scratch);
+    const int kind = key_kind(key);
+    if (!small.empty()) {
+        uint32_t *ids = reinterpret_cast<uint32_t *>(base + L.ids);
+        ce = cudaMemcpyAsync(ids, small.data(), 4 * small.size(), cudaMemcpyHostToDevice, s);
+        if (ce != cudaSuccess) return cuda_fail(ce, "segment ids");
+        SingleArgs a{d_keys_in, d_keys_out, d_values_in, d_values_out, 0, begin_bit, end_bit, kind,
+                     descending ? 1 : 0};
+        a.seg_begin = d_begin_offsets;
+        a.seg_end = d_end_offsets;
+        a.seg_ids = ids;
+        a.seg_count = uint32_t(small.size());
+        {
+            LaunchScope scope(RSORT_KERNEL_SINGLE_TILE, s);
+            ce = launch_single_tile(kb, int(value_bytes), a, s);
+        }
+        if (ce != cudaSuccess) return cuda_fail(ce, "segmented single-tile launch");
+        // ids must outlive the launch's read of them: the stream orders it
+        // before any later reuse of the scratch.
+        ce = cudaStreamSynchronize(s);
+        if (ce != cudaSuccess) return cuda_fail(ce, "segmented single-tile launch");
+    }
+    if (!large.empty()) {
+        Controls c{reinterpret_cast<uint64_t *>(base + L.bins), L.c.bins,
+                   reinterpret_cast<int32_t *>(base + L.lookback), L.c.lookback,
+                   reinterpret_cast<int32_t *>(base + L.counters), L.c.counters};
+        if (L.c.counters) {
+            ce = cudaMemsetAsync(c.counters, 0, 4 * L.c.counters, s);
+            if (ce != cudaSuccess) return cuda_fail(ce, "segmented sort counters");
+        }
+        char *sk = base + L.keys;
+        char *sv = base + L.values;
+        for (size_t i : large) {
+            const size_t len = size_t(e[i] - b[i]);
+            char *ok = static_cast<char *>(d_keys_out) + b[i] * kb;
+            char *ov = value_bytes ? static_cast<char *>(d_values_out) + b[i] * value_bytes : nullptr;
+            ce = cudaMemcpyAsync(ok, static_cast<const char *>(d_keys_in) + b[i] * kb, len * kb,
+                                 cudaMemcpyDeviceToDevice, s);
+            if (ce == cudaSuccess && value_bytes)
+                ce = cudaMemcpyAsync(ov, static_cast<const char *>(d_values_in) + b[i] * value_bytes,
+                                     len * value_bytes, cudaMemcpyDeviceToDevice, s);
+            if (ce != cudaSuccess) return cuda_fail(ce, "segment copy");
+            // The look-back region must have this segment's exact length
+            // (the LengthMismatch rule): pass that prefix of the scratch.
+            rsort_controls cs{};
+            st = rsort_controls_query(key, value_bytes, len, &cs);
+            if (st != RSORT_OK) return st;
+            const Controls cseg{c.bins, cs.bins, c.lookback, cs.lookback, c.counters, cs.counters};
+            int cur_first = 1;
+            st = sort_buffer(key, descending, ok, sk, ov, value_bytes ? sv : nullptr, value_bytes, len,
+                             begin_bit, end_bit, &cur_first, cseg, s);
+            if (st != RSORT_OK) return st;
+            if (!cur_first) {
+                ce = cudaMemcpyAsync(ok, sk, len * kb, cudaMemcpyDeviceToDevice, s);
+                if (ce == cudaSuccess && value_bytes)
+                    ce = cudaMemcpyAsync(ov, sv, len * value_bytes, cudaMemcpyDeviceToDevice, s);
+                if (ce != cudaSuccess) return cuda_fail(ce, "segment copy back");
+            }
+        }
+    }
+    return RSORT_OK;
+}
+
+// ---------------------------------------------------------------------------
 // Lexicographic record sort (rccl-thrust/src/record_sort.rs:144-300)
 // ---------------------------------------------------------------------------
 namespace {

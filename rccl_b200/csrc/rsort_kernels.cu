@@ -568,10 +568,17 @@ __global__ void __launch_bounds__(SINGLE_THREADS, 1) single_tile_kernel(SingleAr
 
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t seg = warp * 32 * ITEMS;
-    const uint32_t n = a.n;
+    uint64_t base = 0;
+    uint32_t n = a.n;
+    if (a.seg_ids) {
+        const uint32_t s = a.seg_ids[blockIdx.x];
+        base = a.seg_begin[s];
+        const uint64_t len = a.seg_end[s] - base;
+        n = len < uint64_t(S::TILE_MAX) ? uint32_t(len) : uint32_t(S::TILE_MAX);
+    }
     const KeyXform asc{a.kind, 0};
-    const B *kin = static_cast<const B *>(a.keys_in);
-    const VT *vin = static_cast<const VT *>(a.values_in);
+    const B *kin = static_cast<const B *>(a.keys_in) + base;
+    const VT *vin = VB > 0 ? static_cast<const VT *>(a.values_in) + base : nullptr;
 
     B key[ITEMS];
     VT val[VB > 0 ? ITEMS : 1];
@@ -632,8 +639,8 @@ __global__ void __launch_bounds__(SINGLE_THREADS, 1) single_tile_kernel(SingleAr
         __syncthreads();
     }
 
-    B *kout = static_cast<B *>(a.keys_out);
-    VT *vout = static_cast<VT *>(a.values_out);
+    B *kout = static_cast<B *>(a.keys_out) + base;
+    VT *vout = VB > 0 ? static_cast<VT *>(a.values_out) + base : nullptr;
 #pragma unroll
     for (int j = 0; j < ITEMS; ++j) {
         const uint32_t pos = seg + j * 32 + lane;
@@ -691,7 +698,7 @@ cudaError_t single_t(const SingleArgs &a, cudaStream_t s) {
     auto k = single_tile_kernel<B, VB>;
     cudaError_t e = ensure_smem(k, S::BYTES);
     if (e != cudaSuccess) return e;
-    k<<<1, SINGLE_THREADS, S::BYTES, s>>>(a);
+    k<<<a.seg_ids ? a.seg_count : 1u, SINGLE_THREADS, S::BYTES, s>>>(a);
     return cudaGetLastError();
 }
 

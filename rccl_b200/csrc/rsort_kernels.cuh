@@ -106,6 +106,13 @@ struct SingleArgs {
     uint32_t n;
     uint32_t begin_bit, end_bit;
     int kind, desc;
+    // Segmented sort: when seg_ids is set, seg_count CTAs run and CTA b
+    // sorts segment s = seg_ids[b], items [seg_begin[s], seg_end[s]) of the
+    // arrays above (at most the single-tile extent); n is unused.
+    const uint64_t *seg_begin = nullptr;
+    const uint64_t *seg_end = nullptr;
+    const uint32_t *seg_ids = nullptr;
+    uint32_t seg_count = 0;
 };
 
 // Host-side launchers (defined in rsort_kernels.cu).  Each returns the CUDA

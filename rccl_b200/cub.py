@@ -482,3 +482,62 @@ def device_merge_pairs(launch: Launch, first_keys, first_values, second_keys, se
     """Merge two sorted key/value ranges (dispatch.rs:1913-1960)."""
     _merge(launch, first_keys, first_values, second_keys, second_values, workspace, output_keys,
            output_values, order)
+
+
+# ---------------------------------------------------------------------------
+# Segmented radix sort (no reference counterpart; listed missing there)
+# ---------------------------------------------------------------------------
+def _segmented(launch: Launch, keys_in, keys_out, values_in, values_out, begin_offsets,
+               end_offsets, bit_range: Optional[range], descending: bool) -> None:
+    launch.check(keys_in, keys_out, values_in, values_out, begin_offsets, end_offsets)
+    if keys_out.dtype != keys_in.dtype or keys_out.numel() != keys_in.numel():
+        raise LengthMismatch("segmented keys out", keys_in.numel(), keys_out.numel())
+    code = key_code(keys_in.dtype)
+    n = keys_in.numel()
+    nseg = begin_offsets.numel()
+    if end_offsets.numel() != nseg:
+        raise LengthMismatch("segment end offsets", nseg, end_offsets.numel())
+    if begin_offsets.dtype not in (torch.int64, torch.uint64) or \
+            end_offsets.dtype not in (torch.int64, torch.uint64):
+        raise BadArgument("segment offsets must be 64-bit")
+    vb = 0
+    if values_in is not None:
+        vb = value_bytes_of(values_in)
+        if values_in.shape[0] != n or values_out.shape[0] != n:
+            raise LengthMismatch("segmented values", n, values_in.shape[0])
+    bits = KEY_BITS[keys_in.dtype]
+    rng = bit_range if bit_range is not None else range(0, bits)
+    lib = _lib.lib()
+    nbytes = lib.rsort_segmented_scratch_bytes(code, vb, n, nseg)
+    tmp = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=launch.device)
+    raise_for(lib.rsort_segmented_sort(
+        code, int(descending), keys_in.data_ptr(), keys_out.data_ptr(), _ptr(values_in),
+        _ptr(values_out), vb, n, nseg, begin_offsets.data_ptr(), end_offsets.data_ptr(),
+        rng.start, rng.stop, tmp.data_ptr(), nbytes, launch.handle))
+    # the launches that read the scratch are ordered before its release on
+    # this stream (caching allocator)
+    del tmp
+
+
+def device_segmented_radix_sort_keys(launch: Launch, keys_in, keys_out, begin_offsets,
+                                     end_offsets, bit_range: Optional[range] = None) -> None:
+    """Stable ascending sort of every segment [begin_offsets[i], end_offsets[i])."""
+    _segmented(launch, keys_in, keys_out, None, None, begin_offsets, end_offsets, bit_range, False)
+
+
+def device_segmented_radix_sort_keys_descending(launch: Launch, keys_in, keys_out, begin_offsets,
+                                                end_offsets, bit_range=None) -> None:
+    _segmented(launch, keys_in, keys_out, None, None, begin_offsets, end_offsets, bit_range, True)
+
+
+def device_segmented_radix_sort_pairs(launch: Launch, keys_in, keys_out, values_in, values_out,
+                                      begin_offsets, end_offsets, bit_range=None) -> None:
+    _segmented(launch, keys_in, keys_out, values_in, values_out, begin_offsets, end_offsets,
+               bit_range, False)
+
+
+def device_segmented_radix_sort_pairs_descending(launch: Launch, keys_in, keys_out, values_in,
+                                                 values_out, begin_offsets, end_offsets,
+                                                 bit_range=None) -> None:
+    _segmented(launch, keys_in, keys_out, values_in, values_out, begin_offsets, end_offsets,
+               bit_range, True)
