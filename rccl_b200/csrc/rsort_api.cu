@@ -731,10 +731,6 @@ rsort_status rsort_segmented_sort(rsort_key_t key, int descending, const void *d
             ce = launch_single_tile(kb, int(value_bytes), a, s);
         }
         if (ce != cudaSuccess) return cuda_fail(ce, "segmented single-tile launch");
-        // ids must outlive the launch's read of them: the stream orders it
-        // before any later reuse of the scratch.
-        ce = cudaStreamSynchronize(s);
-        if (ce != cudaSuccess) return cuda_fail(ce, "segmented single-tile launch");
     }
     if (!large.empty()) {
         Controls c{reinterpret_cast<uint64_t *>(base + L.bins), L.c.bins,
