@@ -330,40 +330,18 @@ __device__ __forceinline__ uint32_t match_digit(uint32_t d, bool check_valid) {
 }
 
 // Warp multi-split rank, one item per lane per step, steps in input order.
-// Per step the lanes of each digit find their peer group, the group's leader
-// (its highest lane) reads the warp's running count for the digit and stores
-// it back advanced by the group size with plain shared loads and stores (one
-// leader per digit per step, so no atomic is needed), and every lane takes
-// base + its rank among lower peers.  Shared atomics are slow on sm_100
-// (~6 lanes per clock per SM measured), so the peer search avoids them where
-// it can:
-//   RSORT_RANK_MODE 0: peers via a shared atomicOr of lane bits into the
-//                      warp's 256-word mask array (cleared by the leader)
-//   RSORT_RANK_MODE 1: owner election without atomics: every lane stores its
-//                      lane id to owner[d]; the surviving id names the group
-//                      and five ballots on its bits give the peer mask
-//   RSORT_RANK_MODE 2: as mode 0, with RANK_MASK_SETS mask arrays used in
-//                      rotation: item j ORs into set j % 3 and the leader of
-//                      item j clears its word while item j + 1 runs, after
-//                      the sync that orders it behind every read of it.  One
-//                      __syncwarp per item instead of three.
-// `wmask` is the warp's scratch (mask arrays or owner array).
-#ifndef RSORT_RANK_MODE
-#define RSORT_RANK_MODE 2
-#endif
-constexpr int RANK_MASK_SETS = RSORT_RANK_MODE == 2 ? 3 : 1;
-
-__device__ __forceinline__ uint32_t match_lane_id(uint32_t w, bool valid) {
-    uint32_t peers = __ballot_sync(0xffffffffu, valid);
-    peers = valid ? peers : ~peers;
-#pragma unroll
-    for (int b = 0; b < 5; ++b) {
-        const bool set = (w >> b) & 1u;
-        const uint32_t v = __ballot_sync(0xffffffffu, set);
-        peers &= set ? v : ~v;
-    }
-    return peers;
-}
+// Per step the lanes of each digit find their peer group through a shared
+// atomicOr of lane bits into the warp's 256-word mask array; the group's
+// leader (its highest lane) reads the warp's running count for the digit and
+// stores it back advanced by the group size with plain shared loads and
+// stores (one leader per digit per step, so no atomic is needed), and every
+// lane takes base + its rank among lower peers.  RANK_MASK_SETS mask arrays
+// are used in rotation: item j ORs into set j % 3 and the leader of item j
+// clears its word while item j + 1 runs, after the sync that orders it
+// behind every read of it, so one __syncwarp per item orders everything.
+// (__match_any_sync, an 8-ballot network, owner election by lane-id stores
+// and a three-sync single-array form were all measured slower on sm_100.)
+constexpr int RANK_MASK_SETS = 3;
 
 // rank[j] = digit << 16 | rank of item j among the warp's items of its digit.
 // ALL_VALID: no padding items (full tile), so no per-item validity tests.
@@ -403,41 +381,6 @@ __device__ __forceinline__ void warp_rank_items_or3(DigitAt digit_at, uint32_t (
     // The last item's mask word stays set: the scratch is re-zeroed before
     // the next tile uses it.
     __syncwarp();
-}
-
-template <int ITEMS, typename DigitAt>
-__device__ __forceinline__ void warp_rank_items_or(DigitAt digit_at, uint32_t (&rank)[ITEMS],
-                                                   uint32_t *whist, uint32_t *wmask) {
-    const uint32_t lane = threadIdx.x & 31;
-    const uint32_t lt = lanemask_lt(), bit = 1u << lane;
-    (void)bit;
-#pragma unroll
-    for (int j = 0; j < ITEMS; ++j) {
-        const uint32_t d = digit_at(j);
-        const bool valid = d < RADIX;
-#if RSORT_RANK_MODE == 0
-        if (valid) atomicOr(&wmask[d], bit);
-        __syncwarp();
-        const uint32_t peers = valid ? wmask[d] : 0u;
-#else
-        if (valid) wmask[d] = lane;
-        __syncwarp();
-        const uint32_t owner = valid ? wmask[d] : 0u;
-        const uint32_t peers = match_lane_id(owner, valid);
-#endif
-        __syncwarp();
-        const uint32_t leader = 31 - __clz(peers);
-        uint32_t got = 0;
-        if (valid && lane == leader) {
-            got = whist[d];
-            whist[d] = got + __popc(peers);
-#if RSORT_RANK_MODE == 0
-            wmask[d] = 0;
-#endif
-        }
-        __syncwarp();
-        rank[j] = __shfl_sync(0xffffffffu, got, leader & 31) + __popc(peers & lt);
-    }
 }
 
 // `digit_at(j)` returns item j's digit (INVALID_DIGIT for padding items).

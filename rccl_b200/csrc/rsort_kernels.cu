@@ -216,9 +216,6 @@ __global__ void __launch_bounds__(HIST_THREADS, 1) histogram_kernel(HistArgs a) 
 #ifndef RSORT_MIN_BLOCKS
 #define RSORT_MIN_BLOCKS 2
 #endif
-#ifndef RSORT_COMBINED_OFFSETS
-#define RSORT_COMBINED_OFFSETS 1
-#endif
 constexpr int WHIST_WORDS = RADIX;
 
 template <typename B, int VB, int ITEMS>
@@ -386,11 +383,9 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
         };
 #ifdef RSORT_RANK_BALLOT
         warp_rank_items<ITEMS>(digit_at, rank, whist + warp * RADIX, !FULL);
-#elif RSORT_RANK_MODE == 2
+#else
         warp_rank_items_or3<ITEMS, FULL>(digit_at, rank, whist + warp * WHIST_WORDS,
                                          wmask + warp * RANK_MASK_SETS * RADIX);
-#else
-        warp_rank_items_or<ITEMS>(digit_at, rank, whist + warp * WHIST_WORDS, wmask + warp * RADIX);
 #endif
         __syncthreads();
         const int64_t next = PERSIST ? int64_t(ctl[2]) : tiles;
@@ -398,7 +393,6 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
         // 2. Per-digit tile totals -> look-back aggregate, warp offsets, tile scan.
         uint32_t total = 0;
         uint64_t *my_lb = a.lookback + uint64_t(tile) * RADIX + tid;
-#if RSORT_COMBINED_OFFSETS
         // Each warp's digit counts become absolute tile positions (tile digit
         // start + the counts of that digit in earlier warps), so the scatter
         // needs one shared load per key.
@@ -418,19 +412,6 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
                 run += t;
             }
         }
-#else
-        if (tid < RADIX) {
-#pragma unroll 4
-            for (int w = 0; w < WARPS; ++w) {
-                const uint32_t t = whist[w * RADIX + tid];
-                whist[w * RADIX + tid] = total;
-                total += t;
-            }
-            st_relaxed_gpu(my_lb, lb_word(tile == 0 ? LB_INCLUSIVE : LB_AGGREGATE, a.tag, total));
-        }
-        const uint32_t tile_excl = block_exclusive_scan_256(total, wsums, nullptr);
-        if (tid < RADIX) tstart[tid] = tile_excl;
-#endif
         __syncthreads();
 
         // 3. Scatter keys and values into shared memory at their tile rank.
@@ -438,18 +419,14 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
 #pragma unroll
         for (int j = 0; j < ITEMS; ++j) {
             if (live(j)) {
-#if RSORT_RANK_MODE == 2 && !defined(RSORT_RANK_BALLOT)
+#ifndef RSORT_RANK_BALLOT
                 const uint32_t d = rank[j] >> 16;
                 const uint32_t rj = rank[j] & 0xffffu;
 #else
                 const uint32_t d = digit_k<KIND>(key[j], a.shift, a.mask);
                 const uint32_t rj = rank[j];
 #endif
-#if RSORT_COMBINED_OFFSETS
                 const uint32_t r = whist[warp * RADIX + d] + rj;
-#else
-                const uint32_t r = tstart[d] + whist[warp * RADIX + d] + rj;
-#endif
                 if (r < count) {
                     skey[r] = key[j];
                     if constexpr (VB > 0) sval[r] = val[j];
