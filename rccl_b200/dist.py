@@ -348,11 +348,21 @@ class PeerExchange:
 _PEER: Optional[PeerExchange] = None
 
 
+def _close_at_exit() -> None:
+    # At interpreter exit the CUDA context may already be going away; the
+    # mappings die with the process either way.
+    try:
+        if _PEER is not None:
+            _PEER.close()
+    except Exception:
+        pass
+
+
 def peer_exchange() -> PeerExchange:
     global _PEER
     if _PEER is None:
         _PEER = PeerExchange()
-        atexit.register(_PEER.close)
+        atexit.register(_close_at_exit)
     return _PEER
 
 
