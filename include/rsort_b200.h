@@ -7,7 +7,7 @@
  * RadixPairsKernel (rccl-cub/src/radix.rs:205-362).  Here one C call owns the
  * whole schedule for one sort, so the Rust side replaces the bodies of
  * device_radix_sort_keys_buffer / device_radix_sort_pairs_buffer with a single
- * call each (see INTEGRATION.md for the binding).
+ * call each.
  *
  * Conventions (rccl-cub semantics kept):
  *  - All device memory is owned by the caller (keys, values, scratch and the

@@ -2,6 +2,8 @@
 // pass schedule of one sort.  Replaces the reference's Rust pass control
 // (rccl-cub/src/radix.rs:364-876) together with the kernel-trait seam it
 // drives (rccl-cub/src/radix.rs:205-362).
+#include <cuda.h>
+
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -9,6 +11,7 @@
 #include "../../include/rsort_b200.h"
 #include "rsort_device.cuh"
 #include "rsort_dist.cuh"
+#include "rsort_internal.cuh"
 #include "rsort_kernels.cuh"
 #include "rsort_records.cuh"
 
@@ -40,34 +43,60 @@ cudaEvent_t pooled_event() {
     return e;
 }
 
-struct LaunchScope {
-    ProfiledLaunch rec{};
-    cudaStream_t stream;
-    bool on;
-    LaunchScope(int kernel, cudaStream_t s) : stream(s), on(g_profile) {
-        ++g_launches;
-        if (on) {
-            rec.kernel = kernel;
-            rec.start = pooled_event();
-            rec.stop = pooled_event();
-            cudaEventRecord(rec.start, stream);
-        }
-    }
-    ~LaunchScope() {
-        if (on) {
-            cudaEventRecord(rec.stop, stream);
-            g_profiled.push_back(rec);
-        }
-    }
-};
+}  // namespace
 
-rsort_status fail(rsort_status s, const char *role, size_t expected = 0, size_t actual = 0) {
+namespace rsort {
+
+LaunchScope::LaunchScope(int k, cudaStream_t s) : kernel(k), stream(s), on(g_profile), rec(nullptr) {
+    ++g_launches;
+    if (on) {
+        auto *r = new ProfiledLaunch{k, pooled_event(), pooled_event()};
+        cudaEventRecord(r->start, stream);
+        rec = r;
+    }
+}
+
+LaunchScope::~LaunchScope() {
+    if (on) {
+        auto *r = static_cast<ProfiledLaunch *>(rec);
+        cudaEventRecord(r->stop, stream);
+        g_profiled.push_back(*r);
+        delete r;
+    }
+}
+
+rsort_status record_failure(rsort_status s, const char *role, size_t expected, size_t actual) {
     g_last_error.status = s;
     g_last_error.role = role;
     g_last_error.expected = expected;
     g_last_error.actual = actual;
     g_last_error.begin_bit = g_last_error.end_bit = g_last_error.key_bits = 0;
     return s;
+}
+
+cudaError_t current_context(void **ctx) {
+    using Fn = CUresult (*)(CUcontext *);
+    static Fn fn = nullptr;
+    if (!fn) {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        cudaError_t e = cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q);
+        if (e != cudaSuccess) return e;
+        if (q != cudaDriverEntryPointSuccess || !f) return cudaErrorNotSupported;
+        fn = reinterpret_cast<Fn>(f);
+    }
+    CUcontext c = nullptr;
+    if (fn(&c) != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    *ctx = c;
+    return cudaSuccess;
+}
+
+}  // namespace rsort
+
+namespace {
+
+rsort_status fail(rsort_status s, const char *role, size_t expected = 0, size_t actual = 0) {
+    return record_failure(s, role, expected, actual);
 }
 
 rsort_status fail_bits(unsigned begin, unsigned end, unsigned key_bits) {
@@ -146,6 +175,17 @@ rsort_status device_info(DeviceInfo *out) {
         return fail(RSORT_UNSUPPORTED_TARGET, "radix sort is built for sm_100a (B200) only");
     return RSORT_OK;
 }
+
+}  // namespace
+
+rsort_status rsort::current_sm_count(int *sm_count) {
+    DeviceInfo d;
+    const rsort_status st = device_info(&d);
+    if (st == RSORT_OK) *sm_count = d.sm_count;
+    return st;
+}
+
+namespace {
 
 size_t tiles_for(size_t n, int kb, int vb) {
     const size_t tile = size_t(onesweep_tile(kb, vb));

@@ -1,0 +1,38 @@
+// Host-side helpers shared by the C ABI translation units: the per-thread
+// last-error record, the launch counter and profiling scope, and the
+// per-device attribute cache.  Not part of the public ABI.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/rsort_b200.h"
+
+namespace rsort {
+
+// Records the failure in the calling thread's rsort_last_error record and
+// returns `s`.  `role` must be a static string.
+rsort_status record_failure(rsort_status s, const char *role, size_t expected = 0,
+                            size_t actual = 0);
+
+// Kernel launch bookkeeping: counts the launch and, when profiling is on,
+// brackets it with CUDA events on `stream` (rsort_profile_*).
+struct LaunchScope {
+    int kernel;
+    cudaStream_t stream;
+    bool on;
+    void *rec;
+    LaunchScope(int kernel, cudaStream_t s);
+    ~LaunchScope();
+};
+
+// SM count of the current device; RSORT_UNSUPPORTED_TARGET unless it is an
+// sm_100 part.
+rsort_status current_sm_count(int *sm_count);
+
+// Driver entry point of the current context (cuCtxGetCurrent), as an opaque
+// handle; nullptr when there is none.
+cudaError_t current_context(void **ctx);
+
+}  // namespace rsort

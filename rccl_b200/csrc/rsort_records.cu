@@ -71,8 +71,12 @@ cudaError_t launch_iota(uint32_t *perm, uint64_t n, int sm_count, cudaStream_t s
 
 cudaError_t launch_permute(const void *src, const uint32_t *perm, uint64_t n, size_t item_bytes,
                            void *dst, int sm_count, cudaStream_t s) {
+    // The copy unit must divide the item width and both base addresses: a
+    // 4-byte aligned row array must not be moved with 8-byte accesses.
+    const uint64_t align = uint64_t(item_bytes) | uint64_t(reinterpret_cast<uintptr_t>(src)) |
+                           uint64_t(reinterpret_cast<uintptr_t>(dst));
     int lg = 3;
-    while (lg > 0 && item_bytes % (size_t(1) << lg) != 0) --lg;
+    while (lg > 0 && align % (uint64_t(1) << lg) != 0) --lg;
     const uint32_t units = uint32_t(item_bytes >> lg);
     const unsigned grid = grid_for(n * units, sm_count);
     switch (lg) {

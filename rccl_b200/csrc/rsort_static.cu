@@ -21,8 +21,9 @@
 //    behind: calls whose work overlaps on the GPU (other streams, other host
 //    threads) race on it and must be serialized by the caller
 //  - the first call on each device looks up the array's device address
-//    (cudaGetSymbolAddress) with that device current; make that first call
-//    before any stream capture begins
+//    (cudaGetSymbolAddress) with that device current, and looks it up again
+//    when a different context is current on that device (after a device
+//    reset); make that first call before any stream capture begins
 //  - a bounded device wait that gives up is not reported by this call (the
 //    sticky status word lives in the shared array and is cleared by the next
 //    call); the output is then unspecified
@@ -31,6 +32,7 @@
 #include <mutex>
 
 #include "../../include/rsort_b200.h"
+#include "rsort_internal.cuh"
 #include "rsort_kernels.cuh"
 
 namespace {
@@ -61,22 +63,39 @@ static __device__ __align__(256) unsigned char g_rsort_static_scratch[RSORT_STAT
 
 namespace {
 
+// Cached device address of the array, per device ordinal and the context that
+// was current when it was resolved: a context that is torn down and recreated
+// (cudaDeviceReset) may load the module at another address, so a different
+// current context resolves the address again.
+struct StaticAddress {
+    void *ctx = nullptr;
+    unsigned char *ptr = nullptr;
+};
 std::mutex g_static_mutex;
-unsigned char *g_static_ptr[64] = {};
+StaticAddress g_static_addr[64];
 
-// Once per device, with that device current: resolve the array's device
-// address.
+// Once per device (and context), with that device current: resolve the
+// array's device address.
 rsort_status static_scratch(unsigned char **out) {
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return RSORT_CUDA_ERROR;
+    if (cudaGetDevice(&dev) != cudaSuccess)
+        return rsort::record_failure(RSORT_CUDA_ERROR, "static scratch: cudaGetDevice");
+    if (dev < 0 || dev >= 64)
+        return rsort::record_failure(RSORT_UNSUPPORTED_TARGET, "static scratch: device ordinal");
+    void *ctx = nullptr;
+    if (rsort::current_context(&ctx) != cudaSuccess)
+        return rsort::record_failure(RSORT_CUDA_ERROR, "static scratch: current context");
     std::lock_guard<std::mutex> lock(g_static_mutex);
-    if (!g_static_ptr[dev]) {
+    StaticAddress &a = g_static_addr[dev];
+    if (!a.ptr || a.ctx != ctx) {
         void *p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_rsort_static_scratch);
-        if (e != cudaSuccess || !p) return RSORT_CUDA_ERROR;
-        g_static_ptr[dev] = static_cast<unsigned char *>(p);
+        if (e != cudaSuccess || !p)
+            return rsort::record_failure(RSORT_CUDA_ERROR, "static scratch: cudaGetSymbolAddress");
+        a.ptr = static_cast<unsigned char *>(p);
+        a.ctx = ctx;
     }
-    *out = g_static_ptr[dev];
+    *out = a.ptr;
     return RSORT_OK;
 }
 
@@ -84,16 +103,25 @@ rsort_status static_scratch(unsigned char **out) {
 
 extern "C" rsort_status rsort_keys_static(rsort_key_t key, int descending, void *d_keys, size_t n,
                                           rsort_stream_t stream) {
-    if (int(key) < RSORT_U32 || int(key) > RSORT_F64) return RSORT_BAD_ARGUMENT;
-    if (n > kMaxItems) return RSORT_WORKSPACE_TOO_SMALL;
+    if (int(key) < RSORT_U32 || int(key) > RSORT_F64)
+        return rsort::record_failure(RSORT_BAD_ARGUMENT, "static keys: key type (32/64-bit keys)");
+    if (n > kMaxItems)
+        return rsort::record_failure(RSORT_WORKSPACE_TOO_SMALL,
+                                     "static keys (at most RSORT_STATIC_MAX_ITEMS)", kMaxItems, n);
     if (n == 0) return RSORT_OK;
-    if (!d_keys) return RSORT_BAD_ARGUMENT;
+    if (!d_keys) return rsort::record_failure(RSORT_BAD_ARGUMENT, "static keys: null buffer");
     rsort_controls c{};
     rsort_status st = rsort_controls_query(key, 0, n, &c);
     if (st != RSORT_OK) return st;
-    if (c.lookback * sizeof(int32_t) > kLookbackBytes || c.bins * sizeof(uint64_t) > kBinsBytes ||
-        c.counters * sizeof(int32_t) > kCountersBytes)
-        return RSORT_WORKSPACE_TOO_SMALL;
+    if (c.lookback * sizeof(int32_t) > kLookbackBytes)
+        return rsort::record_failure(RSORT_WORKSPACE_TOO_SMALL, "static keys: look-back region",
+                                     kLookbackBytes, c.lookback * sizeof(int32_t));
+    if (c.bins * sizeof(uint64_t) > kBinsBytes)
+        return rsort::record_failure(RSORT_WORKSPACE_TOO_SMALL, "static keys: bins region",
+                                     kBinsBytes, c.bins * sizeof(uint64_t));
+    if (c.counters * sizeof(int32_t) > kCountersBytes)
+        return rsort::record_failure(RSORT_WORKSPACE_TOO_SMALL, "static keys: counters region",
+                                     kCountersBytes, c.counters * sizeof(int32_t));
     unsigned char *base = nullptr;
     st = static_scratch(&base);
     if (st != RSORT_OK) return st;
@@ -107,7 +135,8 @@ extern "C" rsort_status rsort_keys_static(rsort_key_t key, int descending, void 
     // bins and look-back words).
     if (c.counters) {
         const cudaError_t e = cudaMemsetAsync(counters, 0, c.counters * sizeof(int32_t), s);
-        if (e != cudaSuccess) return RSORT_CUDA_ERROR;
+        if (e != cudaSuccess)
+            return rsort::record_failure(RSORT_CUDA_ERROR, "static keys: counters reset");
     }
     return rsort_keys(key, descending, d_keys, scratch_keys, n, n, c.bins ? bins : nullptr, c.bins,
                       c.lookback ? lookback : nullptr, c.lookback,

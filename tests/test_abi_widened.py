@@ -87,3 +87,18 @@ def test_exchange_entry_points_validate_arguments():
     st = L.rsort_merge_segments(_lib.RSORT_U64, 0, 2, None, None, None, 4, None, None, None,
                                 None, None, 0, ctypes.byref(flag), 0, None)
     assert st == _lib.RSORT_BAD_ARGUMENT
+
+
+def test_static_entry_point_errors_set_last_error():
+    """rsort_keys_static's argument errors are recorded like every other entry
+    point's, before any device work."""
+    n = (1 << 20) + 1
+    assert L.rsort_keys_static(_lib.RSORT_U64, 0, 16, n, None) == _lib.RSORT_WORKSPACE_TOO_SMALL
+    err = _lib.last_error()
+    assert err.status == _lib.RSORT_WORKSPACE_TOO_SMALL
+    assert err.expected == 1 << 20 and err.actual == n
+    assert b"RSORT_STATIC_MAX_ITEMS" in err.role
+    assert L.rsort_keys_static(_lib.RSORT_U8, 0, 16, 100, None) == _lib.RSORT_BAD_ARGUMENT
+    assert _lib.last_error().status == _lib.RSORT_BAD_ARGUMENT
+    assert L.rsort_keys_static(_lib.RSORT_U32, 0, None, 100, None) == _lib.RSORT_BAD_ARGUMENT
+    assert b"null" in _lib.last_error().role

@@ -38,6 +38,25 @@ def test_rows_lexicographic(arity, n):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("arity", [2, 4])
+def test_rows_at_four_byte_offset(arity):
+    """Rows whose base address is 4-byte but not 8-byte aligned (a view that
+    starts one u32 into its allocation): the row permutation must use 4-byte
+    accesses, not the 8-byte accesses an even word count would allow."""
+    rng = np.random.default_rng(11 + arity)
+    n = 30_001
+    rows = rng.integers(0, 5, (n, arity), dtype=np.uint32)
+    perm = expected(rows)
+    flat = torch.zeros(n * arity + 1, dtype=torch.uint32, device="cuda")
+    view = flat[1:].view(n, arity)
+    assert view.data_ptr() % 8 == 4
+    view.copy_(torch.from_numpy(rows))
+    thrust.sort_rows_lexicographic(thrust.Program.load("cuda:0").par(), view)
+    assert np.array_equal(view.cpu().numpy(), rows[perm])
+    assert int(flat[0].item()) == 0
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("dtype", [torch.float64, torch.bool])
 def test_rows_into_with_payload_types(dtype):
     rng = np.random.default_rng(5)

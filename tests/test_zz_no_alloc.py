@@ -6,9 +6,10 @@ while capturing), plugins whose host framework owns all device memory through
 its own pool, and latency-critical loops.  Its scratch is one static device
 array inside the library, shared by every call on a device.
 
-The test compares its output with the regular rsort_keys entry point (which
-takes caller-owned scratch) on two calls in a row, so the second call runs on
-the leftovers of the first.  This file is named to be collected last.
+The tests compare its output bit-exactly with the CPU oracle and with the
+regular rsort_keys entry point (which takes caller-owned scratch) on two calls
+in a row, so the second call runs on the leftovers of the first.  This file is
+named to be collected last.
 """
 import ctypes
 
@@ -16,6 +17,7 @@ import numpy as np
 import pytest
 import torch
 
+from oracle import pyoracle
 from rccl_b200 import _lib, cub
 
 pytestmark = pytest.mark.gpu
@@ -47,6 +49,12 @@ def bits(a):
     return a.view(np.uint32 if a.dtype.itemsize == 4 else np.uint64)
 
 
+def oracle_sort(keys_np, descending):
+    out, _, _, st = pyoracle.radix_sort(keys_np, None, descending, threads=4)
+    assert st == 0
+    return out
+
+
 def test_static_entry_point_matches_regular_sort_twice():
     rng = np.random.default_rng(77)
     # Two calls in a row on the shared static scratch: first a large u64
@@ -55,6 +63,8 @@ def test_static_entry_point_matches_regular_sort_twice():
     second = rng.integers(0, 2**32, 300_001, dtype=np.uint64).astype(np.uint32)
     got1 = static_sort(first, True)
     got2 = static_sort(second, False)
+    assert np.array_equal(got1, oracle_sort(first, True))
+    assert np.array_equal(got2, oracle_sort(second, False))
     assert np.array_equal(got1, regular_sort(first, True))
     assert np.array_equal(got2, regular_sort(second, False))
 
@@ -66,9 +76,11 @@ def test_static_entry_point_float_keys_and_small_inputs():
     f[::41] = 0.0
     f[::43] = np.nan
     for desc in (False, True):
-        assert np.array_equal(bits(static_sort(f, desc)), bits(regular_sort(f, desc)))
+        got = bits(static_sort(f, desc))
+        assert np.array_equal(got, bits(oracle_sort(f, desc)))
+        assert np.array_equal(got, bits(regular_sort(f, desc)))
     small = rng.integers(-50, 50, 4000, dtype=np.int64)
-    assert np.array_equal(static_sort(small, False), regular_sort(small, False))
+    assert np.array_equal(static_sort(small, False), oracle_sort(small, False))
 
 
 def test_static_entry_point_rejects_oversized_input():
@@ -76,3 +88,6 @@ def test_static_entry_point_rejects_oversized_input():
     st = _lib.lib().rsort_keys_static(_lib.RSORT_U32, 0, t.data_ptr(), t.numel(),
                                       torch.cuda.current_stream().cuda_stream)
     assert st == _lib.RSORT_WORKSPACE_TOO_SMALL
+    err = _lib.last_error()
+    assert err.status == _lib.RSORT_WORKSPACE_TOO_SMALL
+    assert err.expected == MAX_ITEMS and err.actual == MAX_ITEMS + 1
