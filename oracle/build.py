@@ -11,7 +11,8 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_build", "liboracle.so")
 SOURCES = [os.path.join(HERE, "radix_oracle.c")]
-DEPS = SOURCES + [os.path.join(HERE, "radix_oracle.h"), os.path.abspath(__file__)]
+CXX_SOURCES = [os.path.join(HERE, "cpu_sorts.cpp")]
+DEPS = SOURCES + CXX_SOURCES + [os.path.join(HERE, "radix_oracle.h"), os.path.abspath(__file__)]
 
 
 def build(force: bool = False) -> str:
@@ -20,8 +21,11 @@ def build(force: bool = False) -> str:
         return OUT
     os.makedirs(os.path.dirname(OUT), exist_ok=True)
     tmp = OUT + ".tmp"
-    subprocess.run(["gcc", "-O2", "-std=c11", "-fPIC", "-shared", "-pthread", "-o", tmp,
-                    *SOURCES], check=True)
+    obj = os.path.join(os.path.dirname(OUT), "radix_oracle.o")
+    subprocess.run(["gcc", "-O2", "-std=c11", "-fPIC", "-pthread", "-c", "-o", obj, *SOURCES],
+                   check=True)
+    subprocess.run(["g++", "-O3", "-std=c++17", "-fPIC", "-shared", "-pthread", "-o", tmp,
+                    obj, *CXX_SOURCES], check=True)
     os.replace(tmp, OUT)
     return OUT
 

@@ -47,6 +47,8 @@ def lib() -> ctypes.CDLL:
         h.orc_stable_order.restype = None
         h.orc_sample_partition.argtypes = [i, i, vp, vp, i, u, i, vp]
         h.orc_sample_partition.restype = i
+        h.orc_cpu_sort.argtypes = [i, i, i, vp, vp, sz, i]
+        h.orc_cpu_sort.restype = i
         _lib = h
     return _lib
 
@@ -104,6 +106,20 @@ def sample_partition(keys: np.ndarray, shard_sizes, samples_per_rank: int,
     if st != 0:
         raise ValueError(f"oracle sample partition failed: {st}")
     return out
+
+
+def cpu_sort(keys: np.ndarray, values: Optional[np.ndarray] = None, descending: bool = False,
+             stable: bool = False, threads: int = 1):
+    """The CPU baseline stand-ins (std::sort / std::stable_sort, chunked over
+    `threads` threads).  Returns sorted copies (keys, values or None)."""
+    kt = key_type_of(keys)
+    k = np.ascontiguousarray(keys).copy()
+    v = None if values is None else np.ascontiguousarray(values, dtype=np.uint32).copy()
+    st = lib().orc_cpu_sort(kt, int(descending), int(stable), k.ctypes.data,
+                            None if v is None else v.ctypes.data, k.shape[0], threads)
+    if st != 0:
+        raise ValueError(f"cpu sort failed: {st}")
+    return k, v
 
 
 def bits_of(arr: np.ndarray) -> np.ndarray:

@@ -83,6 +83,13 @@ void orc_stable_order(const uint64_t *sort_keys, size_t n, unsigned key_bits, in
 int orc_sample_partition(int key_type, int descending, const void *keys, const size_t *shard_sizes,
                          int world, unsigned samples_per_rank, int threads, size_t *out_counts);
 
+/* CPU baseline stand-ins (oracle/cpu_sorts.cpp): std::sort (stable = 0) or
+ * std::stable_sort (stable = 1) by the order image on one thread, or chunked
+ * on `threads` threads with pairwise std::merge rounds.  values: n u32
+ * values moved with their keys, or NULL. */
+int orc_cpu_sort(int key_type, int descending, int stable, void *keys, uint32_t *values,
+                 size_t n, int threads);
+
 #ifdef __cplusplus
 }
 #endif

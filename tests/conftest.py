@@ -8,4 +8,3 @@ if ROOT not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU")
-    config.addinivalue_line("markers", "slow: large-size GPU parity properties")

@@ -3,7 +3,7 @@ unit tests before it is trusted as the checker of the CUDA path."""
 import numpy as np
 import pytest
 
-from helpers import bits, load_cases
+from helpers import bits, load_cases, order_image
 from oracle import pyoracle as O
 
 CASES = load_cases()
@@ -112,3 +112,29 @@ def test_sample_partition_sums_to_total():
     c = np.full(40_000, 9, np.uint32)
     counts_c = O.sample_partition(c, [10_000] * 4, 256)
     assert counts_c.sum() == c.size and counts_c.max() - counts_c.min() < 200
+
+
+@pytest.mark.parametrize("dtype", [np.uint32, np.int32, np.float32, np.uint64, np.int64, np.float64])
+@pytest.mark.parametrize("threads", [1, 3])
+def test_cpu_baseline_stand_ins_agree_with_the_oracle(dtype, threads):
+    """The std::stable_sort stand-ins of the CPU baseline produce the oracle's
+    output (stable radix order); the std::sort one the same order image."""
+    rng = np.random.default_rng(7)
+    n = 50_001
+    if np.dtype(dtype).kind == "f":
+        k = rng.normal(0, 10, n).astype(dtype)
+        k[::9] = -0.0
+        k[::10] = 0.0
+        k[::23] = np.nan
+    else:
+        k = rng.integers(-1000, 1000, n).astype(dtype)
+    v = np.arange(n, dtype=np.uint32)
+    for desc in (False, True):
+        ok, ov, _, _ = O.radix_sort(k, v, desc)
+        ck, cv = O.cpu_sort(k, v, desc, stable=True, threads=threads)
+        assert np.array_equal(O.bits_of(ck), O.bits_of(ok)) and np.array_equal(cv, ov)
+        sk, _ = O.cpu_sort(k, None, desc, stable=True, threads=threads)
+        assert np.array_equal(O.bits_of(sk), O.bits_of(ok))
+        uk, _ = O.cpu_sort(k, None, desc, stable=False, threads=threads)
+        img = order_image(uk, desc)
+        assert np.array_equal(img, order_image(ok, desc))
