@@ -224,6 +224,67 @@ rsort_status rsort_merge_segments(rsort_key_t key, int descending, unsigned runs
                                   rsort_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Whole multi-GPU sample sort behind one call (no reference counterpart; the
+ * survey's rsort_dist_pairs(world, devices, comms, streams, ...)).  The steps
+ * above run with no host code in between except one read of the gathered
+ * bucket bounds (the receive sizes are data dependent):
+ *   local sort (in place in d_keys / d_values) -> samples -> NCCL all-gather
+ *   -> splitters -> bucket bounds -> NCCL all-gather of the bounds ->
+ *   exchange -> stable merge of the W received runs into d_out_*.
+ *
+ * rsort_dist_pairs drives `world` GPUs from one host thread: devices[r],
+ * comms[r] (an ncclComm_t of rank r in a communicator of `world` ranks, for
+ * example from ncclCommInitAll) and streams[r] belong to rank r, as do the
+ * per-rank arrays.  Collectives of all ranks are issued inside one NCCL
+ * group, as NCCL requires for a single thread.  rsort_dist_pairs_rank is the
+ * same sort for one process (or thread) per GPU: each rank calls it with its
+ * own comm and stream.
+ *
+ * value_bytes 0 sorts keys only (d_values / d_out_values may be NULL).
+ * n_local[r] items per rank (any sizes, zero allowed); the global input is
+ * the ranks' shards concatenated in rank order, and the output is its stable
+ * sort, partitioned contiguously: rank r receives n_out[r] items into
+ * d_out_keys[r] / d_out_values[r] (out_capacity[r] items available).  When
+ * any rank's part does not fit, every rank returns RSORT_WORKSPACE_TOO_SMALL
+ * after filling n_out and before the exchange (the inputs are then sorted
+ * locally, which a repeated call with larger outputs accepts).  d_scratch[r] holds
+ * rsort_dist_scratch_bytes(key, value_bytes, n_local[r], out_capacity[r],
+ * world) bytes, 256-byte aligned.  Keys: the six 32/64-bit RadixKey types.
+ *
+ * exchange: RSORT_EXCHANGE_NCCL moves the buckets with grouped
+ * ncclSend/ncclRecv; RSORT_EXCHANGE_PEER (rsort_dist_pairs only) reads them
+ * straight out of the peers' sorted shards with one copy kernel per rank over
+ * NVLink (peer access is enabled by the call; where a pair of devices cannot
+ * access each other it falls back to NCCL), and synchronizes the streams
+ * before returning so no peer read outlives the call.
+ * The NCCL library is resolved at run time (the libnccl.so.2 already loaded
+ * into the process, else the one on the library path); without it these
+ * calls return RSORT_UNSUPPORTED_TARGET.
+ * ------------------------------------------------------------------------- */
+typedef struct ncclComm *rsort_nccl_comm_t; /* the same type as NCCL's ncclComm_t */
+
+typedef enum { RSORT_EXCHANGE_NCCL = 0, RSORT_EXCHANGE_PEER = 1 } rsort_exchange_t;
+
+size_t rsort_dist_scratch_bytes(rsort_key_t key, size_t value_bytes, size_t n_local,
+                                size_t out_capacity, unsigned world);
+
+rsort_status rsort_dist_pairs(rsort_key_t key, int descending, size_t value_bytes, int world,
+                              const int *devices, rsort_nccl_comm_t const *comms,
+                              rsort_stream_t const *streams, void *const *d_keys,
+                              void *const *d_values, const size_t *n_local,
+                              void *const *d_out_keys, void *const *d_out_values,
+                              const size_t *out_capacity, void *const *d_scratch,
+                              const size_t *scratch_bytes, rsort_exchange_t exchange,
+                              size_t *n_out);
+
+rsort_status rsort_dist_pairs_rank(rsort_key_t key, int descending, size_t value_bytes,
+                                   int rank, int world, rsort_nccl_comm_t comm,
+                                   rsort_stream_t stream, void *d_keys, void *d_values,
+                                   size_t n_local, void *d_out_keys, void *d_out_values,
+                                   size_t out_capacity, void *d_scratch, size_t scratch_bytes,
+                                   size_t *n_out);
+
+/* ---------------------------------------------------------------------------
  * DeviceMergeSort / DeviceMerge for named orders.
  *
  * rccl-cub's merge sort and merge (rccl-cub/src/dispatch.rs:170-193,

@@ -69,7 +69,14 @@ EXPORTED_SYMBOLS = (
     "rsort_rows_lexicographic",
     "rsort_segmented_scratch_bytes",
     "rsort_segmented_sort",
+    "rsort_dist_scratch_bytes",
+    "rsort_dist_pairs",
+    "rsort_dist_pairs_rank",
 )
+
+# rsort_exchange_t
+RSORT_EXCHANGE_NCCL = 0
+RSORT_EXCHANGE_PEER = 1
 
 
 class Controls(ctypes.Structure):
@@ -166,6 +173,16 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.rsort_segmented_sort.argtypes = [i, i, vp, vp, vp, vp, sz, sz, sz, vp, vp, u, u, vp, sz,
                                          vp]
     lib.rsort_segmented_sort.restype = i
+    lib.rsort_dist_scratch_bytes.argtypes = [i, sz, sz, sz, u]
+    lib.rsort_dist_scratch_bytes.restype = sz
+    pvp = ctypes.POINTER(vp)
+    psz = ctypes.POINTER(sz)
+    lib.rsort_dist_pairs.argtypes = [i, i, sz, i, ctypes.POINTER(i), pvp, pvp, pvp, pvp, psz, pvp,
+                                     pvp, psz, pvp, psz, i, psz]
+    lib.rsort_dist_pairs.restype = i
+    lib.rsort_dist_pairs_rank.argtypes = [i, i, sz, i, i, vp, vp, vp, vp, sz, vp, vp, sz, vp, sz,
+                                          psz]
+    lib.rsort_dist_pairs_rank.restype = i
 
 
 def lib() -> ctypes.CDLL:

@@ -16,7 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "_lib", "librsort_b200.so")
 SOURCES = ["rsort_kernels.cu", "rsort_dist.cu", "rsort_api.cu", "rsort_static.cu",
-           "rsort_exchange.cu", "rsort_records.cu"]
+           "rsort_exchange.cu", "rsort_records.cu", "rsort_dist_nccl.cu"]
 HEADERS = ["rsort_device.cuh", "rsort_kernels.cuh", "rsort_dist.cuh", "rsort_records.cuh",
            "rsort_internal.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

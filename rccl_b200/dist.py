@@ -222,6 +222,103 @@ def sample_sort(keys: torch.Tensor, values: Optional[torch.Tensor] = None,
     return out
 
 
+# ---------------------------------------------------------------------------
+# The whole sample sort in one C call (rsort_dist_pairs / _rank): no Python
+# between the steps.
+# ---------------------------------------------------------------------------
+def _dist_out(keys: torch.Tensor, values: Optional[torch.Tensor], capacity: int):
+    ok = torch.empty(max(capacity, 1), dtype=keys.dtype, device=keys.device)
+    ov = None
+    if values is not None:
+        ov = torch.empty((max(capacity, 1),) + tuple(values.shape[1:]), dtype=values.dtype,
+                         device=values.device)
+    return ok, ov
+
+
+def _first_capacity(n: int) -> int:
+    """Output capacity of a first attempt: the shard size plus slack for the
+    sampled splitters' imbalance; a call whose part does not fit reports the
+    sizes, and is repeated with exactly those."""
+    return n + n // 8 + 4096
+
+
+def sample_sort_c(keys: torch.Tensor, values: Optional[torch.Tensor], descending: bool,
+                  comm: int, rank: int, world: int, stream=None
+                  ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """This rank's part of the global stable sort, through rsort_dist_pairs_rank
+    (NCCL exchange).  `comm`: this rank's ncclComm_t (rccl_b200.nccl).  Sorts
+    keys / values in place as its first step."""
+    lib = _lib.lib()
+    kc = key_code(keys.dtype)
+    vb = 0 if values is None else value_bytes_of(values)
+    n = keys.numel()
+    stream = stream if stream is not None else torch.cuda.current_stream(keys.device).cuda_stream
+    cap = _first_capacity(n)
+    for _ in range(2):
+        ok, ov = _dist_out(keys, values, cap)
+        nbytes = lib.rsort_dist_scratch_bytes(kc, vb, n, cap, world)
+        scratch = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=keys.device)
+        n_out = ctypes.c_size_t(0)
+        st = lib.rsort_dist_pairs_rank(kc, int(descending), vb, rank, world, comm, stream,
+                                       keys.data_ptr(),
+                                       None if values is None else values.data_ptr(), n,
+                                       ok.data_ptr(), None if ov is None else ov.data_ptr(), cap,
+                                       scratch.data_ptr(), nbytes, ctypes.byref(n_out))
+        if st == _lib.RSORT_WORKSPACE_TOO_SMALL and _lib.last_error().role.startswith(
+                b"dist sort output"):
+            # every rank returned here (they all hold the same table): each
+            # retries with its own part's size
+            cap = max(n_out.value, 1)
+            continue
+        raise_for(st)
+        m = n_out.value
+        return ok[:m], (ov[:m] if ov is not None else None)
+    raise RuntimeError("rsort_dist_pairs_rank: output capacity negotiation failed")
+
+
+def sample_sort_devices(keys: Sequence[torch.Tensor], values: Optional[Sequence[torch.Tensor]],
+                        descending: bool, comms: Sequence[int], exchange: str = "nccl",
+                        streams: Optional[Sequence] = None):
+    """All ranks' parts of the global stable sort of the shards keys[r] (one
+    per device, in rank order), driven from this thread through
+    rsort_dist_pairs.  comms: rccl_b200.nccl.comm_init_all(devices).
+    exchange: "nccl" (grouped send/recv) or "peer" (copy kernels reading the
+    peers' shards).  Returns [(keys_r, values_r or None)]."""
+    lib = _lib.lib()
+    W = len(keys)
+    kc = key_code(keys[0].dtype)
+    vb = 0 if values is None else value_bytes_of(values[0])
+    devs = [k.device.index for k in keys]
+    if streams is None:
+        streams = [torch.cuda.current_stream(k.device).cuda_stream for k in keys]
+    ns = [k.numel() for k in keys]
+    caps = [_first_capacity(max(ns))] * W
+    mode = {"nccl": _lib.RSORT_EXCHANGE_NCCL, "peer": _lib.RSORT_EXCHANGE_PEER}[exchange]
+    VP, SZ = ctypes.c_void_p * W, ctypes.c_size_t * W
+    for _ in range(2):
+        outs = [_dist_out(keys[r], None if values is None else values[r], caps[r])
+                for r in range(W)]
+        sbytes = [lib.rsort_dist_scratch_bytes(kc, vb, ns[r], caps[r], W) for r in range(W)]
+        scr = [torch.empty(max(sbytes[r], 1), dtype=torch.uint8, device=keys[r].device)
+               for r in range(W)]
+        n_out = SZ()
+        st = lib.rsort_dist_pairs(
+            kc, int(descending), vb, W, (ctypes.c_int * W)(*devs), VP(*comms), VP(*streams),
+            VP(*[k.data_ptr() for k in keys]),
+            VP(*[v.data_ptr() for v in values]) if values is not None else None, SZ(*ns),
+            VP(*[o[0].data_ptr() for o in outs]),
+            VP(*[o[1].data_ptr() for o in outs]) if values is not None else None, SZ(*caps),
+            VP(*[t.data_ptr() for t in scr]), SZ(*sbytes), mode, n_out)
+        if st == _lib.RSORT_WORKSPACE_TOO_SMALL and _lib.last_error().role.startswith(
+                b"dist sort output"):
+            caps = [max(int(n_out[r]), 1) for r in range(W)]
+            continue
+        raise_for(st)
+        return [(outs[r][0][:n_out[r]], outs[r][1][:n_out[r]] if values is not None else None)
+                for r in range(W)]
+    raise RuntimeError("rsort_dist_pairs: output capacity negotiation failed")
+
+
 class PeerExchange:
     """Bucket exchange by direct reads of the peers' shards over NVLink.
 
