@@ -275,11 +275,11 @@ def check_keys_only(inp, out, kind: str, descending: bool) -> bool:
     """Bit-exact comparison with an independent stable sort (torch.sort,
     stable=True) of the input's order image."""
     import torch
-    perm = torch.sort(image_i64(inp, kind, descending), stable=True).indices
-    exp = inp[perm]
-    del perm
     w = torch.int32 if inp.element_size() == 4 else torch.int64
-    return bool(torch.equal(exp.view(w), out.view(w)))
+    perm = torch.sort(image_i64(inp, kind, descending), stable=True).indices
+    exp = inp.view(w)[perm]
+    del perm
+    return bool(torch.equal(exp, out.view(w)))
 
 
 def check_pairs_index(workload: Workload, keys, values, mark=None) -> bool:
@@ -923,6 +923,8 @@ EXCHANGE_NAMES = {
     "peer": "first merge round reads the buckets from the peers' shards over NVLink (CUDA IPC)",
     "peer-copy": "copy kernel pulls the buckets over NVLink (CUDA IPC), then local merge",
     "nccl": "NCCL grouped send/recv, then local merge",
+    "c-nccl": "whole sort in one C call per rank (rsort_dist_pairs_rank): NCCL all-gathers, "
+              "grouped ncclSend/ncclRecv, local merge",
 }
 
 
@@ -963,6 +965,16 @@ def run_dist(args, workload: Workload):
     ops = D.CudaLocalOps(launch)
     L = _lib.lib()
     mode = os.environ.get("RSORT_EXCHANGE", "peer")
+    comm = None
+    if mode == "c-nccl":
+        from rccl_b200 import nccl
+        comm = nccl.comm_init_group()
+
+    def global_sort(k, v, timings=None):
+        if comm is not None:
+            return D.sample_sort_c(k, v, workload.desc, comm, rank, world,
+                                   stream=launch.stream.cuda_stream)
+        return D.sample_sort(k, v, workload.desc, ops=ops, timings=timings)
 
     def restore():
         # Regenerate the shard (untimed): every item is a function of its
@@ -971,7 +983,7 @@ def run_dist(args, workload: Workload):
 
     for _ in range(args.warmup):
         restore()
-        out = D.sample_sort(keys, values, workload.desc, ops=ops)
+        out = global_sort(keys, values)
         del out
     torch.cuda.synchronize()
     dist.barrier()
@@ -990,7 +1002,7 @@ def run_dist(args, workload: Workload):
             t1 = torch.cuda.Event(enable_timing=True)
             L.rsort_profile_enable(1)
             t0.record()
-            out = D.sample_sort(keys, values, workload.desc, ops=ops, timings=phases)
+            out = global_sort(keys, values, timings=phases)
             t1.record()
             L.rsort_profile_enable(0)
             torch.cuda.synchronize()
@@ -1022,7 +1034,7 @@ def run_dist(args, workload: Workload):
         ok = bool(torch.all(img[1:] >= img[:-1])) if img.numel() else True
     kind = np.dtype(workload.key).kind
     if ok_k.numel():
-        img_ends = image_i64(ok_k[[0, -1]], kind, workload.desc)
+        img_ends = image_i64(torch.cat([ok_k[:1], ok_k[-1:]]), kind, workload.desc)
         edge = torch.tensor([float(img_ends[0].item()), float(img_ends[1].item()),
                              float(ok_k.numel())], dtype=torch.float64, device=dev)
         exact_edge = torch.stack([img_ends[0], img_ends[1]])
@@ -1084,7 +1096,7 @@ def run_dist(args, workload: Workload):
             dk.copy_(hk, non_blocking=True)
             if dv is not None:
                 dv.copy_(hv, non_blocking=True)
-            rk, rv = D.sample_sort(dk, dv, workload.desc, ops=ops)
+            rk, rv = global_sort(dk, dv)
             host_out(rk).copy_(rk, non_blocking=True)
             nb = rk.numel() * rk.element_size()
             if rv is not None:
@@ -1144,6 +1156,10 @@ def run_dist(args, workload: Workload):
         }
         print(json.dumps(line), flush=True)
     dist.barrier()
+    if comm is not None:
+        torch.cuda.synchronize()
+        from rccl_b200 import nccl
+        nccl.comm_destroy(comm)
     dist.destroy_process_group()
 
 

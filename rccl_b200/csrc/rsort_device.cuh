@@ -367,10 +367,14 @@ __device__ __forceinline__ void warp_rank_items_or3(DigitAt digit_at, uint32_t (
         const uint32_t leader = 31 - __clz(peers);
         const bool is_leader = valid && lane == leader;
         uint32_t got = 0;
+#ifdef RSORT_LEADER_ATOMIC
+        if (is_leader) got = atomicAdd(&whist[d], __popc(peers));
+#else
         if (is_leader) {
             got = whist[d];
             whist[d] = got + __popc(peers);
         }
+#endif
         prev_leader = is_leader;
         prev_d = d;
         // Packed (digit << 16 | rank): the rank within the warp is below

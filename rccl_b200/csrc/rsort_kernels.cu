@@ -250,6 +250,12 @@ template <bool V> struct BoolTag {
 // tiles are larger).  The per-tile body is compiled twice, for full tiles
 // (no per-item bounds tests, fully unrolled write-out) and for the last,
 // partial tile.
+#ifdef RSORT_VALUES_LATE
+constexpr bool VALUES_LATE = true;
+#else
+constexpr bool VALUES_LATE = false;
+#endif
+
 template <typename B, int VB, int ITEMS, int KIND, bool PERSIST>
 __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_kernel(PassArgs a) {
     using L = OnesweepSmem<B, VB, ITEMS>;
@@ -300,6 +306,16 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
     // tile's registers are dead after its scatter on every path.)
     B key[ITEMS];
     VT val[VB > 0 ? ITEMS : 1];
+    auto load_values = [&](int64_t t) {
+        const uint64_t base = t < tiles ? uint64_t(t) * TILE : 0;
+        const uint64_t remain = t < tiles ? a.n - base : 0;
+        const VT *vin = static_cast<const VT *>(a.values_in) + base;
+#pragma unroll
+        for (int j = 0; j < ITEMS; ++j) {
+            const uint32_t pos = seg + j * 32 + lane;
+            if (pos < remain) val[j] = vin[pos];
+        }
+    };
     auto load_tile = [&](int64_t t) {
         const uint64_t base = t < tiles ? uint64_t(t) * TILE : 0;
         const uint64_t remain = t < tiles ? a.n - base : 0;
@@ -314,14 +330,7 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
                 key[j] = pos < remain ? kin[pos] : B(0);
             }
         }
-        if constexpr (VB > 0) {
-            const VT *vin = static_cast<const VT *>(a.values_in) + base;
-#pragma unroll
-            for (int j = 0; j < ITEMS; ++j) {
-                const uint32_t pos = seg + j * 32 + lane;
-                if (pos < remain) val[j] = vin[pos];
-            }
-        }
+        if constexpr (VB > 0 && !VALUES_LATE) load_values(t);
     };
     load_tile(tile);
 
@@ -338,6 +347,7 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
     }
     __syncthreads();
     if (ctl[3]) {
+        if constexpr (VB > 0 && VALUES_LATE) load_values(tile);
         for (;;) {
             const uint64_t base = uint64_t(tile) * TILE;
             const uint64_t remain = a.n - base;
@@ -362,6 +372,7 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
             if (next >= tiles) break;
             tile = next;
             load_tile(tile);
+            if constexpr (VB > 0 && VALUES_LATE) load_values(tile);
         }
         return;
     }
@@ -414,10 +425,13 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
         }
         __syncthreads();
 
-        // 3. Scatter keys and values into shared memory at their tile rank.
+        // 3. Scatter keys (and, unless they come late, values) into shared
+        //    memory at their tile rank; rank[j] becomes the tile position
+        //    (or ~0 for an item that has none).
         bool bad = false;
 #pragma unroll
         for (int j = 0; j < ITEMS; ++j) {
+            uint32_t r = ~0u;
             if (live(j)) {
 #ifndef RSORT_RANK_BALLOT
                 const uint32_t d = rank[j] >> 16;
@@ -426,15 +440,21 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
                 const uint32_t d = digit_k<KIND>(key[j], a.shift, a.mask);
                 const uint32_t rj = rank[j];
 #endif
-                const uint32_t r = whist[warp * RADIX + d] + rj;
+                r = whist[warp * RADIX + d] + rj;
                 if (r < count) {
                     skey[r] = key[j];
-                    if constexpr (VB > 0) sval[r] = val[j];
+                    if constexpr (VB > 0 && !VALUES_LATE) sval[r] = val[j];
                 } else {
                     bad = true;
+                    r = ~0u;
                 }
             }
+            rank[j] = r;
         }
+        // Values come after the keys (as in the reference's pairs pass): their
+        // loads are issued here, so their latency overlaps the look-back, and
+        // the key registers are already free.
+        if constexpr (VB > 0 && VALUES_LATE) load_values(tile);
 
         // 4. Look-back for the exclusive prefix of this tile's digits.
         if (tid < RADIX) {
@@ -446,7 +466,22 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
                 if (gave_up) ctl[1] = 1;
             }
             gbase[tid] = int64_t(a.bins[tid] + excl) - int64_t(tile_excl);
+#ifdef RSORT_TILE_RANGE_CHECK
+            // Every destination gbase[d] + i (i < count) must lie in [0, n):
+            // true for all digits of a consistent pass, so one test per digit
+            // replaces a test per key.
+            const int64_t g = gbase[tid];
+            if (g < 0 || uint64_t(g) + count > a.n) ctl[1] = 2;
+#endif
         }
+        if constexpr (VB > 0 && VALUES_LATE) {
+#pragma unroll
+            for (int j = 0; j < ITEMS; ++j)
+                if (rank[j] != ~0u) sval[rank[j]] = val[j];
+        }
+#ifdef RSORT_TILE_RANGE_CHECK
+        if (bad) ctl[1] = 2;
+#endif
         __syncthreads();
         const bool abort = ctl[1] != 0;
 
@@ -462,12 +497,17 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
                 const B k = skey[i];
                 const uint32_t d = digit_k<KIND>(k, a.shift, a.mask);
                 const uint64_t dst = uint64_t(gbase[d] + int64_t(i));
+#ifdef RSORT_TILE_RANGE_CHECK
+                kout[dst] = LAST ? from_ordered_k<KIND>(k, dmask) : k;
+                if constexpr (VB > 0) vout[dst] = sval[i];
+#else
                 if (dst < a.n) {
                     kout[dst] = LAST ? from_ordered_k<KIND>(k, dmask) : k;
                     if constexpr (VB > 0) vout[dst] = sval[i];
                 } else {
                     bad = true;
                 }
+#endif
             };
             if constexpr (FULL) {
                 // Fully unrolled unless the next tile's keys are already
@@ -485,7 +525,11 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
             else
                 write_out(BoolTag<false>{});
         }
+#ifdef RSORT_TILE_RANGE_CHECK
+        if (tid == 0 && ctl[1] == 2) atomicExch(a.status, DEV_STATUS_BOUNDS);
+#else
         if (bad) atomicExch(a.status, DEV_STATUS_BOUNDS);
+#endif
         return next;
     };
 
