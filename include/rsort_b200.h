@@ -223,6 +223,23 @@ rsort_status rsort_merge_segments(rsort_key_t key, int descending, unsigned runs
                                   int *result_in_scratch, unsigned first_pair,
                                   rsort_stream_t stream);
 
+/* Single-pass stable merge of `runs` sorted runs (1..64; ties keep the lower
+ * run first), for the last step of the sample sort.  Host arrays of run
+ * pointers (this GPU's memory or a peer's) and lengths; out_* receive the
+ * merged items.  Every run contributes a pivot every S items; a binary search
+ * per pivot and run places the pivots in merged order, and one CTA merges the
+ * runs' segments between consecutive pivots in shared memory, so every item
+ * is read once and written once (the pairwise rsort_merge_runs reads and
+ * writes everything log2(runs) times).  d_scratch: 8-byte aligned,
+ * rsort_multiway_scratch_bytes(key, value_bytes, runs, total items) bytes. */
+size_t rsort_multiway_scratch_bytes(rsort_key_t key, size_t value_bytes, unsigned runs,
+                                    size_t total);
+rsort_status rsort_merge_multiway(rsort_key_t key, int descending, unsigned runs,
+                                  const void *const *run_keys, const void *const *run_values,
+                                  const size_t *run_lengths, size_t value_bytes, void *out_keys,
+                                  void *out_values, void *d_scratch, size_t scratch_bytes,
+                                  rsort_stream_t stream);
+
 /* ---------------------------------------------------------------------------
  * Whole multi-GPU sample sort behind one call (no reference counterpart; the
  * survey's rsort_dist_pairs(world, devices, comms, streams, ...)).  The steps

@@ -72,6 +72,8 @@ EXPORTED_SYMBOLS = (
     "rsort_dist_scratch_bytes",
     "rsort_dist_pairs",
     "rsort_dist_pairs_rank",
+    "rsort_multiway_scratch_bytes",
+    "rsort_merge_multiway",
 )
 
 # rsort_exchange_t
@@ -183,6 +185,10 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.rsort_dist_pairs_rank.argtypes = [i, i, sz, i, i, vp, vp, vp, vp, sz, vp, vp, sz, vp, sz,
                                           psz]
     lib.rsort_dist_pairs_rank.restype = i
+    lib.rsort_multiway_scratch_bytes.argtypes = [i, sz, u, sz]
+    lib.rsort_multiway_scratch_bytes.restype = sz
+    lib.rsort_merge_multiway.argtypes = [i, i, u, pvp, pvp, psz, sz, vp, vp, vp, sz, vp]
+    lib.rsort_merge_multiway.restype = i
 
 
 def lib() -> ctypes.CDLL:

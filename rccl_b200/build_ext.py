@@ -16,9 +16,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "_lib", "librsort_b200.so")
 SOURCES = ["rsort_kernels.cu", "rsort_dist.cu", "rsort_api.cu", "rsort_static.cu",
-           "rsort_exchange.cu", "rsort_records.cu", "rsort_dist_nccl.cu"]
+           "rsort_exchange.cu", "rsort_records.cu", "rsort_dist_nccl.cu",
+           "rsort_multiway.cu"]
 HEADERS = ["rsort_device.cuh", "rsort_kernels.cuh", "rsort_dist.cuh", "rsort_records.cuh",
-           "rsort_internal.cuh"]
+           "rsort_internal.cuh", "rsort_multiway.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2"]
 

@@ -88,6 +88,8 @@ bool value_ok(size_t vb) { return vb == 0 || vb == 1 || vb == 2 || vb == 4 || vb
 
 // Byte offsets of the regions of one rank's scratch.
 struct Layout {
+    // sort_keys / sort_values: the local sort's scratch, then the received
+    // runs; parts: the multiway merge's pivot table (nparts bytes)
     size_t sort_keys, sort_values, bins, lookback, counters, samples, gathered, splitters,
         bounds, all_bounds, parts, total;
     rsort_controls controls;
@@ -118,8 +120,8 @@ bool layout(rsort_key_t key, size_t vb, size_t n_local, size_t cap, unsigned wor
     L->splitters = take(size_t(world > 1 ? world - 1 : 1) * RSORT_COMPOSITE_BYTES);
     L->bounds = take(8 * size_t(world + 2));
     L->all_bounds = take(8 * size_t(world + 2) * world);
-    L->nparts = rsort_merge_partition_words(cap);
-    L->parts = take(8 * (L->nparts ? L->nparts : 1));
+    L->nparts = rsort_multiway_scratch_bytes(key, vb, world, cap);
+    L->parts = take(L->nparts ? L->nparts : 8);
     L->total = off;
     L->controls = c;
     L->S = S;
@@ -143,6 +145,10 @@ struct Rank {
     size_t n_out = 0;
     uint64_t cap_word = 0;  // host copy of cap, gathered with the bounds
 };
+
+// The receive area of the exchange: the local sort's scratch, free again.
+char *recv_keys(Rank &r) { return r.scratch + r.L.sort_keys; }
+char *recv_values(Rank &r) { return r.scratch + r.L.sort_values; }
 
 // Step 1: local stable sort in place, then this rank's regular samples.
 rsort_status local_sort_and_samples(rsort_key_t key, int desc, size_t vb, unsigned world,
@@ -245,10 +251,10 @@ rsort_status exchange_keep(size_t kb, size_t vb, unsigned world, Rank &r) {
     const size_t so = r.send_start[r.rank];
     (void)world;
     if (!keep) return RSORT_OK;
-    cudaError_t e = cudaMemcpyAsync(r.out_keys + roff * kb, r.keys + so * kb, keep * kb,
+    cudaError_t e = cudaMemcpyAsync(recv_keys(r) + roff * kb, r.keys + so * kb, keep * kb,
                                     cudaMemcpyDeviceToDevice, r.stream);
     if (e == cudaSuccess && vb)
-        e = cudaMemcpyAsync(r.out_values + roff * vb, r.values + so * vb, keep * vb,
+        e = cudaMemcpyAsync(recv_values(r) + roff * vb, r.values + so * vb, keep * vb,
                             cudaMemcpyDeviceToDevice, r.stream);
     return e == cudaSuccess ? RSORT_OK
                             : record_failure(RSORT_CUDA_ERROR, "dist sort: local bucket copy");
@@ -270,10 +276,10 @@ rsort_status exchange_nccl(const Nccl &nc, size_t kb, size_t vb, unsigned world,
                                 r.stream);
             }
             if (e == ncclSuccess && r.recv[q]) {
-                e = nc.recv(r.out_keys + roff * kb, r.recv[q] * kb, ncclUint8, int(q), r.comm,
+                e = nc.recv(recv_keys(r) + roff * kb, r.recv[q] * kb, ncclUint8, int(q), r.comm,
                             r.stream);
                 if (e == ncclSuccess && vb)
-                    e = nc.recv(r.out_values + roff * vb, r.recv[q] * vb, ncclUint8, int(q),
+                    e = nc.recv(recv_values(r) + roff * vb, r.recv[q] * vb, ncclUint8, int(q),
                                 r.comm, r.stream);
             }
             if (e != ncclSuccess) return nccl_fail(e, "dist sort: bucket send/recv");
@@ -298,34 +304,29 @@ rsort_status exchange_peer(size_t kb, size_t vb, unsigned world, std::vector<Ran
             src[q] = bytes[q] ? (which ? ranks[q].values : ranks[q].keys) + start * w : nullptr;
         }
         const rsort_status st = rsort_gather_segments(world, src.data(), bytes.data(),
-                                                      which ? r.out_values : r.out_keys,
+                                                      which ? recv_values(r) : recv_keys(r),
                                                       reinterpret_cast<rsort_stream_t>(r.stream));
         if (st != RSORT_OK) return st;
     }
     return RSORT_OK;
 }
 
-// Step 4: stable merge of the W received runs (held back to back in out),
-// result left in out.
+// Step 4: one stable W-way merge of the received runs (back to back in the
+// receive area, in source-rank order) into the output.
 rsort_status merge_received(rsort_key_t key, int desc, size_t kb, size_t vb, unsigned world,
                             Rank &r) {
     if (r.n_out == 0) return RSORT_OK;
-    int in_scratch = 0;
-    rsort_status st = rsort_merge_runs(
-        key, desc, r.out_keys, vb ? r.out_values : nullptr, vb, r.recv.data(), world,
-        r.scratch + r.L.sort_keys, vb ? r.scratch + r.L.sort_values : nullptr,
-        reinterpret_cast<uint64_t *>(r.scratch + r.L.parts), r.L.nparts, &in_scratch,
-        reinterpret_cast<rsort_stream_t>(r.stream));
-    if (st != RSORT_OK) return st;
-    if (in_scratch) {
-        cudaError_t e = cudaMemcpyAsync(r.out_keys, r.scratch + r.L.sort_keys, r.n_out * kb,
-                                        cudaMemcpyDeviceToDevice, r.stream);
-        if (e == cudaSuccess && vb)
-            e = cudaMemcpyAsync(r.out_values, r.scratch + r.L.sort_values, r.n_out * vb,
-                                cudaMemcpyDeviceToDevice, r.stream);
-        if (e != cudaSuccess) return record_failure(RSORT_CUDA_ERROR, "dist sort: merge copy");
+    std::vector<const void *> rk(world), rv(world);
+    size_t off = 0;
+    for (unsigned q = 0; q < world; ++q) {
+        rk[q] = recv_keys(r) + off * kb;
+        rv[q] = vb ? recv_values(r) + off * vb : nullptr;
+        off += r.recv[q];
     }
-    return RSORT_OK;
+    return rsort_merge_multiway(key, desc, world, rk.data(), vb ? rv.data() : nullptr,
+                                r.recv.data(), vb, r.out_keys, vb ? r.out_values : nullptr,
+                                r.scratch + r.L.parts, r.L.nparts,
+                                reinterpret_cast<rsort_stream_t>(r.stream));
 }
 
 rsort_status check_rank_args(rsort_key_t key, size_t vb, const Rank &r, size_t scratch_bytes,

@@ -12,7 +12,9 @@ One process per GPU.  Rank r holds a contiguous shard of the global input.
      each rank pulls its bucket out of every peer's shard with one copy
      kernel over NVLink peer memory (PeerExchange); NCCL grouped send/recv
      is the fallback when the shards cannot be exported
-  7. stable merge of the W received runs (device merge-path kernel)
+  7. one stable W-way merge of the W received runs (rsort_merge_multiway;
+     in the default "peer" mode it reads the buckets straight out of the
+     peers' shards, so the exchange and the merge are one pass)
 The composite order is the global stable order, so the ranks' outputs,
 concatenated in rank order, are the stable sort of the concatenated input.
 
@@ -99,24 +101,46 @@ class CudaLocalOps:
     def merge_runs(self, keys: torch.Tensor, values: Optional[torch.Tensor],
                    run_lengths: Sequence[int], descending: bool
                    ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+        """One stable W-way merge of the runs held back to back in keys /
+        values (ties keep the lower run first) into new tensors."""
         runs = len(run_lengths)
         if runs <= 1:
             return keys, values
-        sk = torch.empty_like(keys)
-        sv = torch.empty_like(values) if values is not None else None
-        nparts = _lib.lib().rsort_merge_partition_words(keys.numel())
-        parts = torch.empty(nparts, dtype=torch.int64, device=keys.device)
-        lens = (ctypes.c_size_t * runs)(*[int(x) for x in run_lengths])
-        in_scratch = ctypes.c_int(0)
+        kb = keys.element_size()
         vb = 0 if values is None else value_bytes_of(values)
-        raise_for(_lib.lib().rsort_merge_runs(
-            key_code(keys.dtype), int(descending), keys.data_ptr(),
-            None if values is None else values.data_ptr(), vb, lens, runs, sk.data_ptr(),
-            None if sv is None else sv.data_ptr(), parts.data_ptr(), nparts,
-            ctypes.byref(in_scratch), self.launch.handle))
-        if in_scratch.value:
-            return sk, sv
-        return keys, values
+        kp, vp, off = [], [], 0
+        for n in run_lengths:
+            kp.append(keys.data_ptr() + off * kb if n else None)
+            vp.append(values.data_ptr() + off * vb if (n and values is not None) else None)
+            off += int(n)
+        return multiway_merge(keys, values, kp, vp, run_lengths, descending, self.launch.handle)
+
+
+def multiway_merge(keys: torch.Tensor, values: Optional[torch.Tensor], key_ptrs, value_ptrs,
+                   run_lengths: Sequence[int], descending: bool, stream):
+    """rsort_merge_multiway of runs given by device pointers (this GPU's memory
+    or a peer's) into new tensors shaped like keys / values."""
+    runs = len(run_lengths)
+    total = int(sum(run_lengths))
+    out_k = torch.empty(total, dtype=keys.dtype, device=keys.device)
+    out_v = None
+    vb = 0
+    if values is not None:
+        vb = value_bytes_of(values)
+        out_v = torch.empty((total,) + tuple(values.shape[1:]), dtype=values.dtype,
+                            device=values.device)
+    if total == 0:
+        return out_k, out_v
+    lib = _lib.lib()
+    kc = key_code(keys.dtype)
+    nbytes = lib.rsort_multiway_scratch_bytes(kc, vb, runs, total)
+    scratch = torch.empty(max(nbytes, 8), dtype=torch.uint8, device=keys.device)
+    VP, SZ = ctypes.c_void_p * runs, ctypes.c_size_t * runs
+    raise_for(lib.rsort_merge_multiway(
+        kc, int(descending), runs, VP(*key_ptrs), VP(*value_ptrs) if values is not None else None,
+        SZ(*[int(x) for x in run_lengths]), vb, out_k.data_ptr(),
+        None if out_v is None else out_v.data_ptr(), scratch.data_ptr(), nbytes, stream))
+    return out_k, out_v
 
 
 # ---------------------------------------------------------------------------
@@ -395,8 +419,9 @@ class PeerExchange:
             raise_for(_lib.lib().rsort_gather_segments(world, srcs, lens, out.data_ptr(), stream))
 
     def merge(self, keys, values, table, sizes, rank: int, world: int, stream, descending):
-        """Merge this rank's W buckets straight out of the shards (peers' over
-        NVLink, the local one from HBM) into new tensors."""
+        """One W-way merge of this rank's W buckets straight out of the shards
+        (peers' over NVLink, the local one from HBM) into new tensors: each
+        bucket crosses NVLink once, inside the merge."""
         hw = _lib.IPC_HANDLE_BYTES // 8
         kb = keys.element_size()
         vb = value_bytes_of(values) if values is not None else 0
@@ -416,22 +441,7 @@ class PeerExchange:
                     col = world + 1 + which * (hw + 1)
                     handle = table[q, col:col + hw].numpy().tobytes()
                     arr[q] = self._base(handle) + int(table[q, col + hw]) + start * width
-        out_k = torch.empty(n_out, dtype=keys.dtype, device=keys.device)
-        sk = torch.empty_like(out_k)
-        out_v = sv = None
-        if values is not None:
-            shape = (n_out,) + tuple(values.shape[1:])
-            out_v = torch.empty(shape, dtype=values.dtype, device=values.device)
-            sv = torch.empty_like(out_v)
-        nparts = _lib.lib().rsort_merge_partition_words(n_out)
-        parts = torch.empty(max(nparts, 1), dtype=torch.int64, device=keys.device)
-        in_scratch = ctypes.c_int(0)
-        raise_for(_lib.lib().rsort_merge_segments(
-            key_code(keys.dtype), int(descending), world, kp, vp, lens, vb, out_k.data_ptr(),
-            None if out_v is None else out_v.data_ptr(), sk.data_ptr(),
-            None if sv is None else sv.data_ptr(), parts.data_ptr(), nparts,
-            ctypes.byref(in_scratch), rank // 2, stream))
-        return (sk, sv) if in_scratch.value else (out_k, out_v)
+        return multiway_merge(keys, values, list(kp), list(vp), list(lens), descending, stream)
 
     def close(self) -> None:
         with self._lock:

@@ -54,14 +54,14 @@ def test_merge_gets_each_peers_bucket(monkeypatch):
     seen = {}
 
     class FakeLib:
-        def rsort_merge_partition_words(self, n):
-            return 4
+        def rsort_multiway_scratch_bytes(self, key, vb, runs, total):
+            return 64
 
-        def rsort_merge_segments(self, key, desc, runs, kp, vp, lens, vb, ok, ov, sk, sv, parts,
-                                 nparts, flag, first_pair, stream):
+        def rsort_merge_multiway(self, key, desc, runs, kp, vp, lens, vb, ok, ov, scratch,
+                                 nbytes, stream):
             seen.update(runs=runs, kp=[kp[i] for i in range(runs)],
                         vp=[vp[i] for i in range(runs)], lens=[lens[i] for i in range(runs)],
-                        vb=vb, first_pair=first_pair)
+                        vb=vb)
             return 0
 
     monkeypatch.setattr(_lib, "lib", lambda: FakeLib())
@@ -69,7 +69,7 @@ def test_merge_gets_each_peers_bucket(monkeypatch):
     values = torch.zeros(sum(sizes[rank]), dtype=torch.int32)
     out_k, out_v = px.merge(keys, values, table, sizes, rank, world, None, False)
     assert out_k.numel() == sum(sizes[q][rank] for q in range(world)) == 17
-    assert seen["runs"] == world and seen["vb"] == 4 and seen["first_pair"] == rank // 2
+    assert seen["runs"] == world and seen["vb"] == 4
     assert seen["lens"] == [7, 4, 6]
     for q in range(world):
         start = sum(sizes[q][:rank])
