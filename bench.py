@@ -768,19 +768,25 @@ def thrust_call_cost(args, workload: Workload, keys_h, values_h, dev, device_ms:
             "timing": "host wall clock around the synchronous call, inputs resident"}
 
 
+E2E_COPY_STREAMS = 4
+
+
 def run_e2e(args, workload: Workload, keys_h, values_h, dev):
     """Public API end to end, as a streaming pipeline: every step copies its
     input from pinned host memory, sorts it through the public API and copies
     the result back to pinned host memory.  Three device input buffers let
     step i+1's upload overlap step i's sort and download (PCIe is full
-    duplex) without waiting for step i-1's download."""
+    duplex) without waiting for step i-1's download.  Each copy is split into
+    E2E_COPY_STREAMS chunks on as many streams, so several copy engines share
+    it."""
     import torch
     from rccl_b200 import thrust
 
     execution = thrust.Program.load(dev).par()
     stream = execution.stream
-    in_s = torch.cuda.Stream(dev)
-    out_s = torch.cuda.Stream(dev)
+    C = E2E_COPY_STREAMS
+    in_s = [torch.cuda.Stream(dev) for _ in range(C)]
+    out_s = [torch.cuda.Stream(dev) for _ in range(C)]
     hk = torch.from_numpy(keys_h).pin_memory()
     ok_ = torch.empty_like(hk).pin_memory()
     NB = 3
@@ -792,38 +798,48 @@ def run_e2e(args, workload: Workload, keys_h, values_h, dev):
         ov = torch.empty_like(hv).pin_memory()
         dvs = [torch.empty(hv.shape, dtype=hv.dtype, device=dev) for _ in range(NB)]
     h2d = hk.numel() * hk.element_size() + (hv.numel() * hv.element_size() if hv is not None else 0)
-    uploaded = [torch.cuda.Event() for _ in range(NB)]
+    n = hk.numel()
+    bounds = [n * c // C for c in range(C + 1)]
+    uploaded = [[torch.cuda.Event() for _ in range(C)] for _ in range(NB)]
     sorted_ = [torch.cuda.Event() for _ in range(NB)]
-    downloaded = [torch.cuda.Event() for _ in range(NB)]
+    downloaded = [[torch.cuda.Event() for _ in range(C)] for _ in range(NB)]
 
     def upload(i):
         b = i % NB
-        in_s.wait_event(downloaded[b])  # the buffer's previous result is out
-        with torch.cuda.stream(in_s):
-            dks[b].copy_(hk, non_blocking=True)
-            if hv is not None:
-                dvs[b].copy_(hv, non_blocking=True)
-        uploaded[b].record(in_s)
+        for c in range(C):
+            lo, hi = bounds[c], bounds[c + 1]
+            for e in downloaded[b]:
+                in_s[c].wait_event(e)  # the buffer's previous result is out
+            with torch.cuda.stream(in_s[c]):
+                dks[b][lo:hi].copy_(hk[lo:hi], non_blocking=True)
+                if hv is not None:
+                    dvs[b][lo:hi].copy_(hv[lo:hi], non_blocking=True)
+            uploaded[b][c].record(in_s[c])
 
     def sort(i):
         b = i % NB
         dk, dv = dks[b], dvs[b]
-        stream.wait_event(uploaded[b])
+        for e in uploaded[b]:
+            stream.wait_event(e)
         thrust_sort(execution, dk, dv, workload.desc)
         sorted_[b].record(stream)
 
     def download(i):
         b = i % NB
-        out_s.wait_event(sorted_[b])
-        with torch.cuda.stream(out_s):
-            ok_.copy_(dks[b], non_blocking=True)
-            if ov is not None:
-                ov.copy_(dvs[b], non_blocking=True)
-        downloaded[b].record(out_s)
+        for c in range(C):
+            lo, hi = bounds[c], bounds[c + 1]
+            out_s[c].wait_event(sorted_[b])
+            with torch.cuda.stream(out_s[c]):
+                ok_[lo:hi].copy_(dks[b][lo:hi], non_blocking=True)
+                if ov is not None:
+                    ov[lo:hi].copy_(dvs[b][lo:hi], non_blocking=True)
+            downloaded[b][c].record(out_s[c])
 
     def pipeline(steps, t0=None, t1=None):
         if t0 is not None:
-            t0.record(in_s)
+            t0.record(in_s[0])
+            for c in range(1, C):
+                in_s[c].wait_event(t0)
         upload(0)
         for i in range(steps):
             if i + 1 < steps:
@@ -831,7 +847,9 @@ def run_e2e(args, workload: Workload, keys_h, values_h, dev):
             sort(i)
             download(i)
         if t1 is not None:
-            t1.record(out_s)
+            for c in range(1, C):
+                out_s[0].wait_event(downloaded[(steps - 1) % NB][c])
+            t1.record(out_s[0])
         torch.cuda.synchronize()
 
     steps = max(3, min(args.steps, 6))
@@ -848,7 +866,8 @@ def run_e2e(args, workload: Workload, keys_h, values_h, dev):
     return {"value": workload.n / (ms / 1e3), "unit": UNIT, "ms_per_step": ms,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": h2d, "steps": steps,
             "output_checked": ok,
-            "pipelined": "step i+1's upload overlaps step i's sort and download",
+            "pipelined": (f"step i+1's upload overlaps step i's sort and download; each copy "
+                          f"split over {C} streams"),
             "api": thrust_api_name(workload, values_h is None)}
 
 

@@ -47,7 +47,11 @@ __device__ __forceinline__ uint64_t mw_count_before(const B *run, uint64_t len, 
     return lo;
 }
 
-template <typename B>
+// Pivot p of the table: its run s, its index k*S, and the counts of every
+// run's items before it.  MAXW > 0: the W - 1 binary searches advance level
+// by level together, with one load per run in flight at a time (W <= MAXW,
+// registers); MAXW == 0: one search after another (any W).
+template <typename B, int MAXW>
 __global__ void multiway_pivot_kernel(MultiwayArgs a) {
     const uint64_t p = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     const uint32_t W = a.runs;
@@ -61,17 +65,58 @@ __global__ void multiway_pivot_kernel(MultiwayArgs a) {
     const uint64_t k = p - a.pivot_start[s];
     const KeyXform xf{a.kind, a.desc};
     const uint64_t x = mw_image(static_cast<const B *>(a.keys[s])[k * a.stride], xf);
-    uint64_t c[MW_MAX_RUNS];
     uint64_t q = k;
-    for (uint32_t t = 0; t < W; ++t) {
-        if (t == s) {
-            c[t] = k * a.stride;
-            continue;
+    if constexpr (MAXW > 0) {
+        uint64_t lo[MAXW], hi[MAXW];
+        const B *run[MAXW];
+#pragma unroll
+        for (int t = 0; t < MAXW; ++t) {
+            lo[t] = 0;
+            hi[t] = (uint32_t(t) < W && uint32_t(t) != s) ? a.len[t] : 0;
+            run[t] = uint32_t(t) < W ? static_cast<const B *>(a.keys[t]) : nullptr;
         }
-        c[t] = mw_count_before(static_cast<const B *>(a.keys[t]), a.len[t], x, t < s, xf);
-        q += (c[t] + a.stride - 1) / a.stride;
+        for (;;) {
+            bool any = false;
+            uint64_t v[MAXW];
+#pragma unroll
+            for (int t = 0; t < MAXW; ++t)
+                if (lo[t] < hi[t]) v[t] = mw_image(run[t][lo[t] + ((hi[t] - lo[t]) >> 1)], xf);
+#pragma unroll
+            for (int t = 0; t < MAXW; ++t) {
+                if (lo[t] < hi[t]) {
+                    const uint64_t mid = lo[t] + ((hi[t] - lo[t]) >> 1);
+                    const bool before = uint32_t(t) < s ? v[t] <= x : v[t] < x;
+                    if (before)
+                        lo[t] = mid + 1;
+                    else
+                        hi[t] = mid;
+                    any = true;
+                }
+            }
+            if (!any) break;
+        }
+#pragma unroll
+        for (int t = 0; t < MAXW; ++t) {
+            if (uint32_t(t) >= W) break;
+            const uint64_t c = uint32_t(t) == s ? k * a.stride : lo[t];
+            if (uint32_t(t) != s) q += (c + a.stride - 1) / a.stride;
+            lo[t] = c;
+        }
+#pragma unroll
+        for (int t = 0; t < MAXW; ++t)
+            if (uint32_t(t) < W) a.table[q * W + t] = lo[t];
+    } else {
+        uint64_t c[MW_MAX_RUNS];
+        for (uint32_t t = 0; t < W; ++t) {
+            if (t == s) {
+                c[t] = k * a.stride;
+                continue;
+            }
+            c[t] = mw_count_before(static_cast<const B *>(a.keys[t]), a.len[t], x, t < s, xf);
+            q += (c[t] + a.stride - 1) / a.stride;
+        }
+        for (uint32_t t = 0; t < W; ++t) a.table[q * W + t] = c[t];
     }
-    for (uint32_t t = 0; t < W; ++t) a.table[q * W + t] = c[t];
 }
 
 template <int VB> struct MwValue;
@@ -242,7 +287,14 @@ template <typename B, int VB>
 cudaError_t multiway_t(MultiwayArgs &a, cudaStream_t s) {
     using S = MwShape<B, VB>;
     const uint32_t piv_blocks = uint32_t((a.pivots + 1 + 255) / 256);
-    multiway_pivot_kernel<B><<<piv_blocks, 256, 0, s>>>(a);
+    if (a.runs <= 2)
+        multiway_pivot_kernel<B, 2><<<piv_blocks, 256, 0, s>>>(a);
+    else if (a.runs <= 4)
+        multiway_pivot_kernel<B, 4><<<piv_blocks, 256, 0, s>>>(a);
+    else if (a.runs <= 8)
+        multiway_pivot_kernel<B, 8><<<piv_blocks, 256, 0, s>>>(a);
+    else
+        multiway_pivot_kernel<B, 0><<<piv_blocks, 256, 0, s>>>(a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     auto k = multiway_merge_kernel<B, VB>;

@@ -465,6 +465,16 @@ def _close_at_exit() -> None:
         pass
 
 
+def release_peer_mappings() -> None:
+    """Unmap every peer shard this process mapped for the peer exchange.  The
+    mappings are cached across calls (up to PeerExchange.CACHE of them), so a
+    peer's freed shard stays mapped, and its memory held, until it is evicted,
+    this is called, or the process exits.  Call it between sorts only, after
+    the collective that ends a sort; the next sort maps again."""
+    if _PEER is not None:
+        _PEER.close()
+
+
 def peer_exchange() -> PeerExchange:
     global _PEER
     if _PEER is None:
