@@ -89,7 +89,7 @@ bool value_ok(size_t vb) { return vb == 0 || vb == 1 || vb == 2 || vb == 4 || vb
 // Byte offsets of the regions of one rank's scratch.
 struct Layout {
     // sort_keys / sort_values: the local sort's scratch, then the received
-    // runs; parts: the multiway merge's pivot table (nparts bytes)
+    // runs; parts: the merge-path partitions (nparts words)
     size_t sort_keys, sort_values, bins, lookback, counters, samples, gathered, splitters,
         bounds, all_bounds, parts, total;
     rsort_controls controls;
@@ -120,8 +120,8 @@ bool layout(rsort_key_t key, size_t vb, size_t n_local, size_t cap, unsigned wor
     L->splitters = take(size_t(world > 1 ? world - 1 : 1) * RSORT_COMPOSITE_BYTES);
     L->bounds = take(8 * size_t(world + 2));
     L->all_bounds = take(8 * size_t(world + 2) * world);
-    L->nparts = rsort_multiway_scratch_bytes(key, vb, world, cap);
-    L->parts = take(L->nparts ? L->nparts : 8);
+    L->nparts = rsort_merge_partition_words(cap);
+    L->parts = take(8 * (L->nparts ? L->nparts : 1));
     L->total = off;
     L->controls = c;
     L->S = S;
@@ -311,22 +311,32 @@ rsort_status exchange_peer(size_t kb, size_t vb, unsigned world, std::vector<Ran
     return RSORT_OK;
 }
 
-// Step 4: one stable W-way merge of the received runs (back to back in the
-// receive area, in source-rank order) into the output.
+// Step 4: stable merge of the received runs (back to back in the receive
+// area, in source-rank order; ties keep the lower rank) into the output:
+// pairwise merge-path rounds between the receive area and the output, the
+// last round landing in the output (one copy when the run count makes the
+// rounds end in the receive area).  Measured faster on B200 than one W-way
+// pass (rsort_merge_multiway) for these local runs.
 rsort_status merge_received(rsort_key_t key, int desc, size_t kb, size_t vb, unsigned world,
                             Rank &r) {
+    (void)world;
     if (r.n_out == 0) return RSORT_OK;
-    std::vector<const void *> rk(world), rv(world);
-    size_t off = 0;
-    for (unsigned q = 0; q < world; ++q) {
-        rk[q] = recv_keys(r) + off * kb;
-        rv[q] = vb ? recv_values(r) + off * vb : nullptr;
-        off += r.recv[q];
+    rsort_stream_t rs = reinterpret_cast<rsort_stream_t>(r.stream);
+    int in_scratch = 0;
+    rsort_status st = rsort_merge_runs(
+        key, desc, recv_keys(r), vb ? recv_values(r) : nullptr, vb, r.recv.data(), world,
+        r.out_keys, vb ? r.out_values : nullptr, reinterpret_cast<uint64_t *>(r.scratch + r.L.parts),
+        r.L.nparts, &in_scratch, rs);
+    if (st != RSORT_OK) return st;
+    if (!in_scratch) {  // the result is in the receive area
+        cudaError_t e = cudaMemcpyAsync(r.out_keys, recv_keys(r), r.n_out * kb,
+                                        cudaMemcpyDeviceToDevice, r.stream);
+        if (e == cudaSuccess && vb)
+            e = cudaMemcpyAsync(r.out_values, recv_values(r), r.n_out * vb,
+                                cudaMemcpyDeviceToDevice, r.stream);
+        if (e != cudaSuccess) return record_failure(RSORT_CUDA_ERROR, "dist sort: merge copy");
     }
-    return rsort_merge_multiway(key, desc, world, rk.data(), vb ? rv.data() : nullptr,
-                                r.recv.data(), vb, r.out_keys, vb ? r.out_values : nullptr,
-                                r.scratch + r.L.parts, r.L.nparts,
-                                reinterpret_cast<rsort_stream_t>(r.stream));
+    return RSORT_OK;
 }
 
 rsort_status check_rank_args(rsort_key_t key, size_t vb, const Rank &r, size_t scratch_bytes,

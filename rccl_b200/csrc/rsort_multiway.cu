@@ -147,26 +147,36 @@ __global__ void __launch_bounds__(MW_THREADS) multiway_merge_kernel(MultiwayArgs
     using VT = typename MwValue<VB>::type;
     constexpr int ITEMS = S::ITEMS;
     extern __shared__ __align__(16) uint8_t smem[];
-    B *kbuf[2] = {reinterpret_cast<B *>(smem + S::K0), reinterpret_cast<B *>(smem + S::K1)};
-    VT *vbuf[2] = {reinterpret_cast<VT *>(smem + S::V0), reinterpret_cast<VT *>(smem + S::V1)};
+    B *const kb0 = reinterpret_cast<B *>(smem + S::K0);
+    B *const kb1 = reinterpret_cast<B *>(smem + S::K1);
+    VT *const vb0 = reinterpret_cast<VT *>(smem + S::V0);
+    VT *const vb1 = reinterpret_cast<VT *>(smem + S::V1);
     const B **kseg = reinterpret_cast<const B **>(smem + S::BND);          // [W] segment starts
     const VT **vseg = reinterpret_cast<const VT **>(kseg + MW_MAX_RUNS);    // [W]
     uint32_t *bnd = reinterpret_cast<uint32_t *>(vseg + MW_MAX_RUNS);       // [W + 1] offsets
+    __shared__ uint64_t lo_row[MW_MAX_RUNS], len_row[MW_MAX_RUNS];
     __shared__ uint64_t out_base;
     const uint32_t W = a.runs, tid = threadIdx.x;
     const KeyXform xf{a.kind, a.desc};
     const uint64_t r0 = uint64_t(blockIdx.x) * a.group;
     const uint64_t r1 = r0 + a.group < a.pivots ? r0 + a.group : a.pivots;
+    // The table rows are read by W threads at once; one thread then turns the
+    // segment lengths into offsets.
+    if (tid < W) {
+        const uint64_t lo = a.table[r0 * W + tid], hi = a.table[r1 * W + tid];
+        lo_row[tid] = lo;
+        len_row[tid] = hi - lo;
+        kseg[tid] = static_cast<const B *>(a.keys[tid]) + lo;
+        vseg[tid] = VB > 0 ? static_cast<const VT *>(a.values[tid]) + lo : nullptr;
+    }
+    __syncthreads();
     if (tid == 0) {
         uint64_t base = 0;
         uint32_t off = 0;
         for (uint32_t t = 0; t < W; ++t) {
-            const uint64_t lo = a.table[r0 * W + t], hi = a.table[r1 * W + t];
-            kseg[t] = static_cast<const B *>(a.keys[t]) + lo;
-            vseg[t] = VB > 0 ? static_cast<const VT *>(a.values[t]) + lo : nullptr;
             bnd[t] = off;
-            off += uint32_t(hi - lo);
-            base += lo;
+            off += uint32_t(len_row[t]);
+            base += lo_row[t];
         }
         bnd[W] = off;
         out_base = base;
@@ -196,8 +206,8 @@ __global__ void __launch_bounds__(MW_THREADS) multiway_merge_kernel(MultiwayArgs
         for (int u = 0; u < ITEMS; ++u) {
             const uint32_t i = tid + uint32_t(u) * MW_THREADS;
             if (i < n) {
-                kbuf[0][i] = kr[u];
-                if constexpr (VB > 0) vbuf[0][i] = vr[u];
+                kb0[i] = kr[u];
+                if constexpr (VB > 0) vb0[i] = vr[u];
             }
         }
     }
@@ -208,17 +218,63 @@ __global__ void __launch_bounds__(MW_THREADS) multiway_merge_kernel(MultiwayArgs
     int cur = 0;
     uint32_t segs = W;
     while (segs > 1) {
-        const B *ik = kbuf[cur];
-        const VT *iv = vbuf[cur];
-        B *ok = kbuf[cur ^ 1];
-        VT *ov = vbuf[cur ^ 1];
+        const B *ik = cur ? kb1 : kb0;
+        const VT *iv = cur ? vb1 : vb0;
+        B *ok = cur ? kb0 : kb1;
+        VT *ov = cur ? vb0 : vb1;
         const uint32_t o0 = tid * ITEMS;
-        uint32_t o = o0;
         const uint32_t oend = o0 + ITEMS < n ? o0 + ITEMS : n;
+        const uint32_t npairs = (segs + 1) >> 1;
+        // Fast path: the thread's outputs lie in one merge pair, so the merge
+        // is a fixed, unrolled ITEMS-step loop (as in the two-run merge).
+        bool done = o0 >= n;
+        if (!done) {
+            uint32_t pr = 0;
+            while (pr + 1 < npairs && bnd[2 * pr + 2] <= o0) ++pr;
+            const uint32_t sa = 2 * pr;
+            const uint32_t a0 = bnd[sa], a1 = bnd[sa + 1];
+            const uint32_t b1 = sa + 1 < segs ? bnd[sa + 2] : a1;
+            if (oend <= b1 && b1 > a1) {
+                const uint32_t la = a1 - a0, lb = b1 - a1;
+                const B *ta = ik + a0;
+                const B *tb = ik + a1;
+                const uint32_t diag = o0 - a0;
+                uint32_t lo = diag > lb ? diag - lb : 0, hi = diag < la ? diag : la;
+                while (lo < hi) {
+                    const uint32_t mid = (lo + hi) >> 1;
+                    if (mw_image(ta[mid], xf) <= mw_image(tb[diag - 1 - mid], xf))
+                        lo = mid + 1;
+                    else
+                        hi = mid;
+                }
+                uint32_t ia = lo, ib = diag - lo;
+                uint64_t ima = ia < la ? mw_image(ta[ia], xf) : 0;
+                uint64_t imb = ib < lb ? mw_image(tb[ib], xf) : 0;
+#pragma unroll
+                for (int k = 0; k < ITEMS; ++k) {
+                    const bool take_a = ib >= lb || (ia < la && ima <= imb);
+                    const uint32_t src = take_a ? a0 + ia : a1 + ib;
+                    if (o0 + k < oend) {
+                        ok[o0 + k] = ik[src];
+                        if constexpr (VB > 0) ov[o0 + k] = iv[src];
+                    }
+                    if (take_a) {
+                        ++ia;
+                        if (ia < la) ima = mw_image(ta[ia], xf);
+                    } else {
+                        ++ib;
+                        if (ib < lb) imb = mw_image(tb[ib], xf);
+                    }
+                }
+                done = true;
+            }
+        }
+        // General path: outputs that cross a pair boundary, or a lone
+        // segment's copy.
+        uint32_t o = done ? oend : o0;
         while (o < oend) {
             // the pair (segments 2pr and 2pr + 1) holding output position o;
             // a lone last segment is a pair without a right side
-            const uint32_t npairs = (segs + 1) >> 1;
             uint32_t pr = 0;
             while (pr + 1 < npairs && bnd[2 * pr + 2] <= o) ++pr;
             const uint32_t sa = 2 * pr;
@@ -275,9 +331,11 @@ __global__ void __launch_bounds__(MW_THREADS) multiway_merge_kernel(MultiwayArgs
 
     B *outk = static_cast<B *>(a.out_keys) + out_base;
     VT *outv = VB > 0 ? static_cast<VT *>(a.out_values) + out_base : nullptr;
+    const B *fk = cur ? kb1 : kb0;
+    const VT *fv = cur ? vb1 : vb0;
     for (uint32_t i = tid; i < n; i += MW_THREADS) {
-        outk[i] = kbuf[cur][i];
-        if constexpr (VB > 0) outv[i] = vbuf[cur][i];
+        outk[i] = fk[i];
+        if constexpr (VB > 0) outv[i] = fv[i];
     }
 }
 

@@ -7,14 +7,20 @@
 namespace rsort {
 
 constexpr int MW_MAX_RUNS = 64;
-constexpr int MW_THREADS = 512;
+#ifndef RSORT_MW_THREADS
+#define RSORT_MW_THREADS 512
+#endif
+constexpr int MW_THREADS = RSORT_MW_THREADS;
 
 // Outputs per thread and merge round; the CTA's capacity is MW_THREADS times
 // this.  Odd, so the serial merges of neighbouring threads (which start this
 // many items apart in shared memory) fall into different banks; smaller for
 // wide items so two buffers still fit in shared memory.
+#ifndef RSORT_MW_ITEMS
+#define RSORT_MW_ITEMS 9
+#endif
 constexpr int mw_items(int key_bytes, int value_bytes) {
-    return key_bytes + value_bytes <= 12 ? 9 : 5;
+    return key_bytes + value_bytes <= 12 ? RSORT_MW_ITEMS : (RSORT_MW_ITEMS + 1) / 2;
 }
 
 struct MultiwayArgs {

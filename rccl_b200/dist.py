@@ -101,11 +101,14 @@ class CudaLocalOps:
     def merge_runs(self, keys: torch.Tensor, values: Optional[torch.Tensor],
                    run_lengths: Sequence[int], descending: bool
                    ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
-        """One stable W-way merge of the runs held back to back in keys /
-        values (ties keep the lower run first) into new tensors."""
+        """Stable merge of the runs held back to back in keys / values (ties
+        keep the lower run first): one W-way merge into new tensors, or, with
+        merge_method() == "tree", pairwise rounds (rsort_merge_runs)."""
         runs = len(run_lengths)
         if runs <= 1:
             return keys, values
+        if merge_method() == "tree":
+            return self._merge_tree(keys, values, run_lengths, descending)
         kb = keys.element_size()
         vb = 0 if values is None else value_bytes_of(values)
         kp, vp, off = [], [], 0
@@ -114,6 +117,37 @@ class CudaLocalOps:
             vp.append(values.data_ptr() + off * vb if (n and values is not None) else None)
             off += int(n)
         return multiway_merge(keys, values, kp, vp, run_lengths, descending, self.launch.handle)
+
+
+    def _merge_tree(self, keys, values, run_lengths, descending):
+        runs = len(run_lengths)
+        sk = torch.empty_like(keys)
+        sv = torch.empty_like(values) if values is not None else None
+        nparts = _lib.lib().rsort_merge_partition_words(keys.numel())
+        parts = torch.empty(max(nparts, 1), dtype=torch.int64, device=keys.device)
+        lens = (ctypes.c_size_t * runs)(*[int(x) for x in run_lengths])
+        in_scratch = ctypes.c_int(0)
+        vb = 0 if values is None else value_bytes_of(values)
+        raise_for(_lib.lib().rsort_merge_runs(
+            key_code(keys.dtype), int(descending), keys.data_ptr(),
+            None if values is None else values.data_ptr(), vb, lens, runs, sk.data_ptr(),
+            None if sv is None else sv.data_ptr(), parts.data_ptr(), nparts,
+            ctypes.byref(in_scratch), self.launch.handle))
+        return (sk, sv) if in_scratch.value else (keys, values)
+
+
+def merge_method() -> str:
+    """How a rank merges its W received runs: "multiway" (one pass,
+    rsort_merge_multiway) or "tree" (pairwise rounds; in the peer exchange the
+    first round reads the peers' shards).  RSORT_MERGE overrides the
+    default."""
+    m = os.environ.get("RSORT_MERGE", DEFAULT_MERGE)
+    if m not in ("multiway", "tree"):
+        raise ValueError(f"RSORT_MERGE={m!r}: expected 'multiway' or 'tree'")
+    return m
+
+
+DEFAULT_MERGE = "tree"
 
 
 def multiway_merge(keys: torch.Tensor, values: Optional[torch.Tensor], key_ptrs, value_ptrs,
@@ -441,7 +475,26 @@ class PeerExchange:
                     col = world + 1 + which * (hw + 1)
                     handle = table[q, col:col + hw].numpy().tobytes()
                     arr[q] = self._base(handle) + int(table[q, col + hw]) + start * width
-        return multiway_merge(keys, values, list(kp), list(vp), list(lens), descending, stream)
+        if merge_method() == "multiway":
+            return multiway_merge(keys, values, list(kp), list(vp), list(lens), descending, stream)
+        # Pairwise: the first round merges bucket pairs straight from the shards,
+        # launched from pair rank // 2 on, so the ranks read different peers.
+        out_k = torch.empty(n_out, dtype=keys.dtype, device=keys.device)
+        sk = torch.empty_like(out_k)
+        out_v = sv = None
+        if values is not None:
+            shape = (n_out,) + tuple(values.shape[1:])
+            out_v = torch.empty(shape, dtype=values.dtype, device=values.device)
+            sv = torch.empty_like(out_v)
+        nparts = _lib.lib().rsort_merge_partition_words(n_out)
+        parts = torch.empty(max(nparts, 1), dtype=torch.int64, device=keys.device)
+        in_scratch = ctypes.c_int(0)
+        raise_for(_lib.lib().rsort_merge_segments(
+            key_code(keys.dtype), int(descending), world, kp, vp, lens, vb, out_k.data_ptr(),
+            None if out_v is None else out_v.data_ptr(), sk.data_ptr(),
+            None if sv is None else sv.data_ptr(), parts.data_ptr(), nparts,
+            ctypes.byref(in_scratch), rank // 2, stream))
+        return (sk, sv) if in_scratch.value else (out_k, out_v)
 
     def close(self) -> None:
         with self._lock:

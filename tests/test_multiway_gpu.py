@@ -9,7 +9,7 @@ import pytest
 import torch
 
 from helpers import bits, order_image
-from rccl_b200 import _lib, cub
+from rccl_b200 import _lib
 from rccl_b200 import dist as D
 
 pytestmark = pytest.mark.gpu
@@ -44,11 +44,15 @@ def merge(runs, desc, vb, device="cuda:0"):
             np.arange(n, dtype=np.uint32)
     tk = torch.from_numpy(keys.copy()).to(device)
     tv = torch.from_numpy(vals.copy()).to(device) if vals is not None else None
-    ops = D.CudaLocalOps(cub.Program.load(device).on())
     lens = [r.size for r in runs]
-    ok, ov = ops.merge_runs(tk, tv, lens, desc) if len(runs) > 1 else (tk, tv)
-    if len(runs) == 1:
-        return keys, vals, tk.cpu().numpy(), (tv.cpu().numpy() if tv is not None else None)
+    kb = tk.element_size()
+    kp, vp, off = [], [], 0
+    for n_ in lens:
+        kp.append(tk.data_ptr() + off * kb if n_ else None)
+        vp.append(tv.data_ptr() + off * vb if (n_ and tv is not None) else None)
+        off += n_
+    ok, ov = D.multiway_merge(tk, tv, kp, vp, lens, desc,
+                              torch.cuda.current_stream(device).cuda_stream)
     torch.cuda.synchronize()
     return keys, vals, ok.cpu().numpy(), (ov.cpu().numpy() if ov is not None else None)
 

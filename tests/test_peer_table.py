@@ -6,6 +6,7 @@ recorders.  The device side runs in the GPU tests."""
 import ctypes
 
 import numpy as np
+import pytest
 import torch
 
 from rccl_b200 import _lib
@@ -40,7 +41,9 @@ def test_record_words_roundtrip(monkeypatch):
     assert rec[2 + HW:2 + 2 * HW].numpy().tobytes() == hv and rec[2 + 2 * HW].item() == 512
 
 
-def test_merge_gets_each_peers_bucket(monkeypatch):
+@pytest.mark.parametrize("method", ["tree", "multiway"])
+def test_merge_gets_each_peers_bucket(monkeypatch, method):
+    monkeypatch.setenv("RSORT_MERGE", method)
     world, rank = 3, 1
     # sizes[q][r]: items of rank q's shard destined to rank r
     sizes = [[5, 7, 2], [3, 4, 9], [0, 6, 1]]
@@ -54,6 +57,16 @@ def test_merge_gets_each_peers_bucket(monkeypatch):
     seen = {}
 
     class FakeLib:
+        def rsort_merge_partition_words(self, n):
+            return 4
+
+        def rsort_merge_segments(self, key, desc, runs, kp, vp, lens, vb, ok, ov, sk, sv, parts,
+                                 nparts, flag, first_pair, stream):
+            seen.update(runs=runs, kp=[kp[i] for i in range(runs)],
+                        vp=[vp[i] for i in range(runs)], lens=[lens[i] for i in range(runs)],
+                        vb=vb, first_pair=first_pair)
+            return 0
+
         def rsort_multiway_scratch_bytes(self, key, vb, runs, total):
             return 64
 
@@ -70,6 +83,8 @@ def test_merge_gets_each_peers_bucket(monkeypatch):
     out_k, out_v = px.merge(keys, values, table, sizes, rank, world, None, False)
     assert out_k.numel() == sum(sizes[q][rank] for q in range(world)) == 17
     assert seen["runs"] == world and seen["vb"] == 4
+    if method == "tree":
+        assert seen["first_pair"] == rank // 2
     assert seen["lens"] == [7, 4, 6]
     for q in range(world):
         start = sum(sizes[q][:rank])
