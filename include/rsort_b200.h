@@ -230,7 +230,9 @@ rsort_status rsort_merge_segments(rsort_key_t key, int descending, unsigned runs
  * per pivot and run places the pivots in merged order, and one CTA merges the
  * runs' segments between consecutive pivots in shared memory, so every item
  * is read once and written once (the pairwise rsort_merge_runs reads and
- * writes everything log2(runs) times).  d_scratch: 8-byte aligned,
+ * writes everything log2(runs) times, but on B200 its two-run kernel keeps
+ * more work in flight and is the faster of the two for runs in this GPU's
+ * memory).  d_scratch: 8-byte aligned,
  * rsort_multiway_scratch_bytes(key, value_bytes, runs, total items) bytes. */
 size_t rsort_multiway_scratch_bytes(rsort_key_t key, size_t value_bytes, unsigned runs,
                                     size_t total);

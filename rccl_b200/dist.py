@@ -12,9 +12,9 @@ One process per GPU.  Rank r holds a contiguous shard of the global input.
      each rank pulls its bucket out of every peer's shard with one copy
      kernel over NVLink peer memory (PeerExchange); NCCL grouped send/recv
      is the fallback when the shards cannot be exported
-  7. one stable W-way merge of the W received runs (rsort_merge_multiway;
-     in the default "peer" mode it reads the buckets straight out of the
-     peers' shards, so the exchange and the merge are one pass)
+  7. stable merge of the W received runs: pairwise merge-path rounds (the
+     default; in "peer" mode the first round reads the buckets straight out
+     of the peers' shards) or one W-way pass (RSORT_MERGE=multiway)
 The composite order is the global stable order, so the ranks' outputs,
 concatenated in rank order, are the stable sort of the concatenated input.
 
