@@ -67,3 +67,15 @@ def test_reference_arm_under_torchrun_uses_the_strong_scaling_config():
     assert line["config"]["workload"].startswith("config 5")
     assert line["scaling"] == "strong" and line["n_gpus"] == 2
     assert line["config"]["per_gpu_n"] == 65536 // 2
+
+
+def test_reference_arm_under_torchrun_uses_the_strong_scaling_config():
+    """With WORLD_SIZE > 1 the reference arm's line carries the same config as
+    the GPU arm's multi-GPU line: config 5, strong scaling."""
+    lines = run(["--impl", "reference", "--gpus", "2", "--n", "65536", "--steps", "1",
+                 "--warmup", "0"], env={"RANK": "0", "WORLD_SIZE": "2"})
+    assert len(lines) == 1
+    line = lines[0]
+    assert line["config"]["workload"].startswith("config 5")
+    assert line["scaling"] == "strong" and line["n_gpus"] == 2
+    assert line["config"]["per_gpu_n"] == 65536 // 2
