@@ -186,7 +186,9 @@ rsort_status rsort_dist_bounds(rsort_key_t key, int descending, const void *d_so
                                size_t m, unsigned rank, const void *d_splitters, unsigned world,
                                uint64_t *d_bounds, rsort_stream_t stream);
 
-/* uint64 words of merge-path partition scratch a merge of `total` items needs. */
+/* uint64 words of merge-path partition scratch a merge of `total` items needs
+ * (rsort_merge, and every round of rsort_merge_runs / rsort_merge_segments,
+ * which launch up to 32 pair merges at once). */
 size_t rsort_merge_partition_words(size_t total);
 
 /* Stable merge of two sorted runs (a then b; equal keys keep a first).

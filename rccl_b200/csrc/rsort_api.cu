@@ -4,6 +4,7 @@
 // drives (rccl-cub/src/radix.rs:205-362).
 #include <cuda.h>
 
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -928,7 +929,12 @@ rsort_status rsort_rows_lexicographic(size_t words, void *d_rows, void *d_payloa
     return e == cudaSuccess ? RSORT_OK : cuda_fail(e, "record sort permutation");
 }
 
-size_t rsort_merge_partition_words(size_t total) { return merge_partition_words(total, 0); }
+// One word per merge tile plus one, and one more per pair of a batched round
+// (rsort_merge_runs / rsort_merge_segments launch up to MERGE_MAX_PAIRS pair
+// merges at once, each with its own closing word).
+size_t rsort_merge_partition_words(size_t total) {
+    return merge_partition_words(total, 0) + MERGE_MAX_PAIRS;
+}
 
 namespace {
 rsort_status merge_impl(rsort_key_t key, int descending, bool total, const void *a_keys,
@@ -987,6 +993,52 @@ rsort_status merge_impl(rsort_key_t key, int descending, bool total, const void 
 }
 }  // namespace
 
+namespace {
+
+// A round of a merge tree: independent two-run merges launched together, at
+// most MERGE_MAX_PAIRS per launch, so every pair (and every peer a pair reads)
+// progresses at once.
+struct PairMerge {
+    const void *ak, *av;
+    size_t na;
+    const void *bk, *bv;
+    size_t nb;
+    void *ok, *ov;
+};
+
+rsort_status merge_round(rsort_key_t key, int descending, const std::vector<PairMerge> &pairs,
+                         size_t value_bytes, uint64_t *d_partitions, size_t npartitions,
+                         cudaStream_t s) {
+    const int kind = key_kind(key);
+    for (size_t first = 0; first < pairs.size(); first += MERGE_MAX_PAIRS) {
+        const size_t count = std::min<size_t>(MERGE_MAX_PAIRS, pairs.size() - first);
+        MergeBatch b{};
+        b.npairs = uint32_t(count);
+        uint64_t words = 0;
+        for (size_t q = 0; q < count; ++q) {
+            const PairMerge &m = pairs[first + q];
+            if (merge_partition_words(m.na, m.nb) > 0x7fffffffull)
+                return fail(RSORT_SIZE_OVERFLOW, "merge tiles");
+            b.pair[q] = MergeArgs{m.ak, m.av, m.na, m.bk, m.bv, m.nb, m.ok, m.ov, kind,
+                                  descending ? 1 : 0};
+            b.split_start[q] = words;
+            words += merge_partition_words(m.na, m.nb);
+        }
+        b.split_start[count] = words;
+        if (!d_partitions || npartitions < words)
+            return fail(RSORT_WORKSPACE_TOO_SMALL, "merge partitions", words, npartitions);
+        cudaError_t e;
+        {
+            LaunchScope scope(RSORT_KERNEL_MERGE, s);
+            e = launch_merge_batch(key_bytes(key), int(value_bytes), b, d_partitions, s);
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "merge launch");
+    }
+    return RSORT_OK;
+}
+
+}  // namespace
+
 rsort_status rsort_merge_runs(rsort_key_t key, int descending, void *keys, void *values,
                               size_t value_bytes, const size_t *run_lengths, unsigned runs,
                               void *scratch_keys, void *scratch_values, uint64_t *d_partitions,
@@ -1001,23 +1053,31 @@ rsort_status rsort_merge_runs(rsort_key_t key, int descending, void *keys, void 
         off[r] = total;
         total += len[r];
     }
-    // Pairwise merge tree: runs (0,1), (2,3), ... each round; ties keep the
-    // lower run first, so the result is stable across runs in run order.
+    *result_in_scratch = 0;
+    if (runs > 1 && total > 0) {
+        if (!keys || !scratch_keys || (value_bytes && (!values || !scratch_values)))
+            return fail(RSORT_BAD_ARGUMENT, "null buffer");
+        DeviceInfo dev;
+        rsort_status st = device_info(&dev);
+        if (st != RSORT_OK) return st;
+    }
+    // Pairwise merge tree: runs (0,1), (2,3), ... each round, one batched
+    // launch per round; ties keep the lower run first, so the result is
+    // stable across runs in run order.
     char *src_k = static_cast<char *>(keys), *dst_k = static_cast<char *>(scratch_keys);
     char *src_v = static_cast<char *>(values), *dst_v = static_cast<char *>(scratch_values);
     bool in_scratch = false;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     while (len.size() > 1) {
         std::vector<size_t> nlen, noff;
+        std::vector<PairMerge> pairs;
         for (size_t r = 0; r < len.size(); r += 2) {
             if (r + 1 < len.size()) {
-                rsort_status st = rsort_merge(
-                    key, descending, src_k + off[r] * kb, value_bytes ? src_v + off[r] * value_bytes : nullptr,
+                pairs.push_back(PairMerge{
+                    src_k + off[r] * kb, value_bytes ? src_v + off[r] * value_bytes : nullptr,
                     len[r], src_k + off[r + 1] * kb,
                     value_bytes ? src_v + off[r + 1] * value_bytes : nullptr, len[r + 1],
-                    dst_k + off[r] * kb, value_bytes ? dst_v + off[r] * value_bytes : nullptr,
-                    value_bytes, d_partitions, npartitions, stream);
-                if (st != RSORT_OK) return st;
+                    dst_k + off[r] * kb, value_bytes ? dst_v + off[r] * value_bytes : nullptr});
                 nlen.push_back(len[r] + len[r + 1]);
             } else {
                 if (len[r]) {
@@ -1033,6 +1093,9 @@ rsort_status rsort_merge_runs(rsort_key_t key, int descending, void *keys, void 
             }
             noff.push_back(off[r]);
         }
+        rsort_status st = merge_round(key, descending, pairs, value_bytes, d_partitions,
+                                      npartitions, s);
+        if (st != RSORT_OK) return st;
         len.swap(nlen);
         off.swap(noff);
         std::swap(src_k, dst_k);
@@ -1060,10 +1123,11 @@ rsort_status rsort_merge_segments(rsort_key_t key, int descending, unsigned runs
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     char *ok = static_cast<char *>(out_keys), *ov = static_cast<char *>(out_values);
     // First round straight from the given runs (a peer's memory is read once,
-    // by the merge itself): pairs (0,1), (2,3), ... into out, launched from
-    // pair first_pair on (wrapping), so ranks that start at different pairs
-    // read different peers at the same time.  The output layout does not
-    // depend on the launch order.
+    // by the merge itself): pairs (0,1), (2,3), ... into out, all in one
+    // batched launch whose blocks interleave the pairs, so every peer is read
+    // at once.  Pairs are listed from first_pair on (wrapping): ranks starting
+    // at different pairs begin their reads on different peers.  The output
+    // layout does not depend on the order.
     const unsigned pairs = (runs + 1) / 2;
     std::vector<size_t> len(pairs), at(pairs);
     size_t off = 0;
@@ -1073,27 +1137,36 @@ rsort_status rsort_merge_segments(rsort_key_t key, int descending, unsigned runs
         at[p] = off;
         off += len[p];
     }
+    if (off > 0) {
+        if (!ok || (value_bytes && !ov)) return fail(RSORT_BAD_ARGUMENT, "null buffer");
+        DeviceInfo dev;
+        rsort_status st = device_info(&dev);
+        if (st != RSORT_OK) return st;
+    }
+    std::vector<PairMerge> first;
     for (unsigned k = 0; k < pairs; ++k) {
         const unsigned p = (first_pair + k) % pairs;
         const unsigned r = 2 * p;
-        const size_t off = at[p];
+        const size_t o = at[p];
         if (r + 1 < runs) {
-            rsort_status st = rsort_merge(key, descending, run_keys[r],
-                                          value_bytes ? run_values[r] : nullptr, run_lengths[r],
-                                          run_keys[r + 1], value_bytes ? run_values[r + 1] : nullptr,
-                                          run_lengths[r + 1], ok + off * kb,
-                                          value_bytes ? ov + off * value_bytes : nullptr,
-                                          value_bytes, d_partitions, npartitions, stream);
-            if (st != RSORT_OK) return st;
+            if ((run_lengths[r] && !run_keys[r]) || (run_lengths[r + 1] && !run_keys[r + 1]))
+                return fail(RSORT_BAD_ARGUMENT, "null run");
+            first.push_back(PairMerge{run_keys[r], value_bytes ? run_values[r] : nullptr,
+                                      run_lengths[r], run_keys[r + 1],
+                                      value_bytes ? run_values[r + 1] : nullptr,
+                                      run_lengths[r + 1], ok + o * kb,
+                                      value_bytes ? ov + o * value_bytes : nullptr});
         } else if (run_lengths[r]) {
-            cudaError_t e = cudaMemcpyAsync(ok + off * kb, run_keys[r], run_lengths[r] * kb,
+            cudaError_t e = cudaMemcpyAsync(ok + o * kb, run_keys[r], run_lengths[r] * kb,
                                             cudaMemcpyDeviceToDevice, s);
             if (e == cudaSuccess && value_bytes)
-                e = cudaMemcpyAsync(ov + off * value_bytes, run_values[r],
+                e = cudaMemcpyAsync(ov + o * value_bytes, run_values[r],
                                     run_lengths[r] * value_bytes, cudaMemcpyDeviceToDevice, s);
             if (e != cudaSuccess) return cuda_fail(e, "merge run copy");
         }
     }
+    rsort_status st = merge_round(key, descending, first, value_bytes, d_partitions, npartitions, s);
+    if (st != RSORT_OK) return st;
     if (len.size() <= 1) return RSORT_OK;
     // Later rounds in local memory, between out and scratch.
     return rsort_merge_runs(key, descending, out_keys, out_values, value_bytes, len.data(),

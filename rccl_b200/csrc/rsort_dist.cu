@@ -144,13 +144,29 @@ __device__ __forceinline__ uint64_t merge_path(const B *a, uint64_t na, const B 
 // Merge-path partitions: split[i] = number of A items among the first
 // i * MERGE_TILE outputs (one thread per tile boundary).
 template <typename B>
+__device__ __forceinline__ uint64_t merge_split(const MergeArgs &p, uint64_t i) {
+    const uint64_t total = p.na + p.nb;
+    const uint64_t diag = i * MERGE_TILE < total ? i * MERGE_TILE : total;
+    return merge_path(static_cast<const B *>(p.a_keys), p.na, static_cast<const B *>(p.b_keys),
+                      p.nb, diag, KeyXform{p.kind, p.desc});
+}
+
+template <typename B>
 __global__ void merge_partition_kernel(MergeArgs p, uint64_t *split, uint64_t nsplit) {
     const uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= nsplit) return;
-    const uint64_t total = p.na + p.nb;
-    const uint64_t diag = i * MERGE_TILE < total ? i * MERGE_TILE : total;
-    split[i] = merge_path(static_cast<const B *>(p.a_keys), p.na, static_cast<const B *>(p.b_keys),
-                          p.nb, diag, KeyXform{p.kind, p.desc});
+    split[i] = merge_split<B>(p, i);
+}
+
+// Partitions of every pair of a batch: pair q's words start at split_start[q].
+template <typename B>
+__global__ void merge_partition_batch_kernel(const __grid_constant__ MergeBatch b,
+                                             uint64_t *split) {
+    const uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= b.split_start[b.npairs]) return;
+    uint32_t q = 0;
+    while (i >= b.split_start[q + 1]) ++q;
+    split[i] = merge_split<B>(b.pair[q], i - b.split_start[q]);
 }
 
 template <typename B, int VB>
@@ -174,7 +190,8 @@ template <> struct MergeValue<16> { using type = uint4; };
 // own merge-path split, gather through shared memory and write the tile out
 // coalesced.
 template <typename B, int VB>
-__global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(MergeArgs p, const uint64_t *split) {
+__device__ __forceinline__ void merge_tile(const MergeArgs &p, const uint64_t *split,
+                                           uint64_t tile) {
     using S = MergeSmem<B, VB>;
     using VT = typename MergeValue<VB>::type;
     extern __shared__ __align__(16) uint8_t smem[];
@@ -186,9 +203,9 @@ __global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(MergeArgs p, const
     const VT *av = static_cast<const VT *>(p.a_values);
     const VT *bv = static_cast<const VT *>(p.b_values);
     const uint64_t total = p.na + p.nb;
-    const uint64_t d0 = uint64_t(blockIdx.x) * MERGE_TILE;
+    const uint64_t d0 = tile * MERGE_TILE;
     const uint64_t d1 = d0 + MERGE_TILE < total ? d0 + MERGE_TILE : total;
-    const uint64_t a0 = split[blockIdx.x], a1 = split[blockIdx.x + 1];
+    const uint64_t a0 = split[tile], a1 = split[tile + 1];
     const uint64_t b0 = d0 - a0, b1 = d1 - a1;
     const uint32_t la = uint32_t(a1 - a0), lb = uint32_t(b1 - b0);
     const uint32_t n = la + lb;
@@ -266,6 +283,23 @@ __global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(MergeArgs p, const
     }
 }
 
+template <typename B, int VB>
+__global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(MergeArgs p, const uint64_t *split) {
+    merge_tile<B, VB>(p, split, blockIdx.x);
+}
+
+// All pairs of a batch in one launch.  Block k merges tile k / npairs of pair
+// k % npairs, so every pair (and every peer a pair reads) progresses at once.
+template <typename B, int VB>
+__global__ void __launch_bounds__(MERGE_THREADS)
+    merge_batch_kernel(const __grid_constant__ MergeBatch b, const uint64_t *split) {
+    const uint32_t q = blockIdx.x % b.npairs;
+    const uint64_t t = blockIdx.x / b.npairs;
+    const uint64_t tiles = b.split_start[q + 1] - b.split_start[q] - 1;
+    if (t >= tiles) return;
+    merge_tile<B, VB>(b.pair[q], split + b.split_start[q], t);
+}
+
 // ---------------------------------------------------------------------------
 // Launchers
 // ---------------------------------------------------------------------------
@@ -288,6 +322,41 @@ cudaError_t merge_t(const MergeArgs &p, uint64_t *split, cudaStream_t s) {
     }
     k<<<dim3(uint32_t(blocks)), MERGE_THREADS, S::BYTES, s>>>(p, split);
     return cudaGetLastError();
+}
+
+template <typename B, int VB>
+cudaError_t merge_batch_t(const MergeBatch &b, uint64_t *split, cudaStream_t s) {
+    using S = MergeSmem<B, VB>;
+    const uint64_t words = b.split_start[b.npairs];
+    uint64_t max_tiles = 0;
+    for (uint32_t q = 0; q < b.npairs; ++q) {
+        const uint64_t t = b.split_start[q + 1] - b.split_start[q] - 1;
+        max_tiles = t > max_tiles ? t : max_tiles;
+    }
+    if (max_tiles == 0) return cudaSuccess;
+    merge_partition_batch_kernel<B><<<dim3(uint32_t((words + 255) / 256)), 256, 0, s>>>(b, split);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    auto k = merge_batch_kernel<B, VB>;
+    if (S::BYTES > 32 * 1024) {
+        e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(S::BYTES));
+        if (e != cudaSuccess) return e;
+    }
+    k<<<dim3(uint32_t(max_tiles * b.npairs)), MERGE_THREADS, S::BYTES, s>>>(b, split);
+    return cudaGetLastError();
+}
+
+template <typename B>
+cudaError_t merge_batch_vb(int vb, const MergeBatch &b, uint64_t *split, cudaStream_t s) {
+    switch (vb) {
+        case 0: return merge_batch_t<B, 0>(b, split, s);
+        case 1: return merge_batch_t<B, 1>(b, split, s);
+        case 2: return merge_batch_t<B, 2>(b, split, s);
+        case 4: return merge_batch_t<B, 4>(b, split, s);
+        case 8: return merge_batch_t<B, 8>(b, split, s);
+        case 16: return merge_batch_t<B, 16>(b, split, s);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 template <typename B>
@@ -353,6 +422,13 @@ cudaError_t launch_merge(int key_bytes, int value_bytes, const MergeArgs &p, uin
                          cudaStream_t s) {
     return key_bytes == 4 ? merge_vb<uint32_t>(value_bytes, p, split, s)
                           : merge_vb<uint64_t>(value_bytes, p, split, s);
+}
+
+cudaError_t launch_merge_batch(int key_bytes, int value_bytes, const MergeBatch &b,
+                               uint64_t *split, cudaStream_t s) {
+    if (b.npairs == 0) return cudaSuccess;
+    return key_bytes == 4 ? merge_batch_vb<uint32_t>(value_bytes, b, split, s)
+                          : merge_batch_vb<uint64_t>(value_bytes, b, split, s);
 }
 
 }  // namespace rsort

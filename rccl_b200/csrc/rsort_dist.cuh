@@ -44,6 +44,18 @@ size_t merge_partition_words(uint64_t na, uint64_t nb);
 cudaError_t launch_merge(int key_bytes, int value_bytes, const MergeArgs &p, uint64_t *split,
                          cudaStream_t s);
 
+// Several independent two-run merges in one launch (a round of a merge tree).
+// Pair q's merge-path partitions take split_start[q + 1] - split_start[q]
+// words (merge_partition_words of the pair) of the split array.
+constexpr uint32_t MERGE_MAX_PAIRS = 32;
+struct MergeBatch {
+    MergeArgs pair[MERGE_MAX_PAIRS];
+    uint64_t split_start[MERGE_MAX_PAIRS + 1];
+    uint32_t npairs;
+};
+cudaError_t launch_merge_batch(int key_bytes, int value_bytes, const MergeBatch &b,
+                               uint64_t *split, cudaStream_t s);
+
 // Segment gather of the bucket exchange: segment q (src[q], a peer's or the
 // local shard) lands at dst + dst_start[q]; unit_log2[q] is the copy width
 // (log2 bytes, at most 4) that divides both addresses and the length.

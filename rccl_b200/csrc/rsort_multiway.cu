@@ -13,12 +13,11 @@
 // fewer than S items, so G consecutive intervals hold at most (W + G) * S
 // items: one CTA merges them in shared memory.
 //
-// Merge.  A tile is G consecutive intervals (rows r0 to r0 + G of the
-// table).  A persistent CTA loads a tile's W segments back to back into
-// shared memory, merges them pairwise in log2(W) rounds between two shared
-// buffers (merge path per thread, ties to the left segment) and writes its
-// output range out coalesced, with the next tile's loads already in flight.
-// The runs are read once and the output written once.
+// Merge.  A CTA loads its G intervals' W segments (row r0 to row r0 + G of
+// the table) back to back into shared memory, merges them pairwise in
+// log2(W) rounds between two shared buffers (merge path per thread, ties to
+// the left segment), and writes its output range out coalesced.  The runs
+// are read once and the output written once.
 #include "../../include/rsort_b200.h"
 #include "rsort_device.cuh"
 #include "rsort_internal.cuh"
@@ -133,32 +132,17 @@ struct MwShape {
     static constexpr int ITEMS = mw_items(int(sizeof(B)), VB);
     static constexpr int CAP = MW_THREADS * ITEMS;
     static constexpr int VSIZE = VB > 0 ? VB : 1;
-    // two buffers (keys, values each)
+    // two buffers (keys, values each), then the segment bounds
     static constexpr size_t K0 = 0;
     static constexpr size_t K1 = K0 + size_t(CAP) * sizeof(B);
     static constexpr size_t V0 = K1 + size_t(CAP) * sizeof(B);
     static constexpr size_t V1 = V0 + (VB > 0 ? size_t(CAP) * VSIZE : 0);
-    static constexpr size_t BYTES = V1 + (VB > 0 ? size_t(CAP) * VSIZE : 0);
+    static constexpr size_t BND = (V1 + (VB > 0 ? size_t(CAP) * VSIZE : 0) + 15) / 16 * 16;
+    static constexpr size_t BYTES = BND + size_t(2 * MW_MAX_RUNS) * 8 + size_t(MW_MAX_RUNS + 1) * 4;
 };
 
-// One tile's description: the W segments (read position in every run) and
-// their offsets in the tile, and the tile's first output position.
-struct MwTile {
-    const void *kseg[MW_MAX_RUNS];
-    const void *vseg[MW_MAX_RUNS];
-    uint32_t bnd[MW_MAX_RUNS + 1];
-    uint64_t out_base;
-};
-
-// Persistent and software-pipelined: a CTA takes tiles g, g + grid, ...; the
-// loads of the next tile are issued into registers before the current tile is
-// merged, so their latency (a peer's memory is microseconds away over NVLink)
-// overlaps the merge and the write-out.  Per tile: the W segments go back to
-// back into buffer 0, pairwise rounds between buffers 0 and 1 merge them
-// (merge path per thread, ties to the left segment), and the result is
-// written out coalesced.
 template <typename B, int VB>
-__global__ void __launch_bounds__(MW_THREADS, 1) multiway_merge_kernel(MultiwayArgs a) {
+__global__ void __launch_bounds__(MW_THREADS) multiway_merge_kernel(MultiwayArgs a) {
     using S = MwShape<B, VB>;
     using VT = typename MwValue<VB>::type;
     constexpr int ITEMS = S::ITEMS;
@@ -167,57 +151,57 @@ __global__ void __launch_bounds__(MW_THREADS, 1) multiway_merge_kernel(MultiwayA
     B *const kb1 = reinterpret_cast<B *>(smem + S::K1);
     VT *const vb0 = reinterpret_cast<VT *>(smem + S::V0);
     VT *const vb1 = reinterpret_cast<VT *>(smem + S::V1);
-    __shared__ MwTile tiles[2];
+    const B **kseg = reinterpret_cast<const B **>(smem + S::BND);          // [W] segment starts
+    const VT **vseg = reinterpret_cast<const VT **>(kseg + MW_MAX_RUNS);    // [W]
+    uint32_t *bnd = reinterpret_cast<uint32_t *>(vseg + MW_MAX_RUNS);       // [W + 1] offsets
     __shared__ uint64_t lo_row[MW_MAX_RUNS], len_row[MW_MAX_RUNS];
+    __shared__ uint64_t out_base;
     const uint32_t W = a.runs, tid = threadIdx.x;
     const KeyXform xf{a.kind, a.desc};
-    const uint64_t groups = (a.pivots + a.group - 1) / a.group;
-
+    const uint64_t r0 = uint64_t(blockIdx.x) * a.group;
+    const uint64_t r1 = r0 + a.group < a.pivots ? r0 + a.group : a.pivots;
     // The table rows are read by W threads at once; one thread then turns the
-    // segment lengths into offsets.  The partition bounds a tile by
-    // (W + G) * S <= CAP items; the clamp only keeps a corrupt table from
-    // overrunning shared memory.
-    auto describe = [&](uint64_t g, MwTile &T) {
-        const uint64_t r0 = g * a.group;
-        const uint64_t r1 = r0 + a.group < a.pivots ? r0 + a.group : a.pivots;
-        if (tid < W) {
-            const uint64_t lo = a.table[r0 * W + tid], hi = a.table[r1 * W + tid];
-            lo_row[tid] = lo;
-            len_row[tid] = hi - lo;
-            T.kseg[tid] = static_cast<const B *>(a.keys[tid]) + lo;
-            T.vseg[tid] = VB > 0 ? static_cast<const VT *>(a.values[tid]) + lo : nullptr;
+    // segment lengths into offsets.
+    if (tid < W) {
+        const uint64_t lo = a.table[r0 * W + tid], hi = a.table[r1 * W + tid];
+        lo_row[tid] = lo;
+        len_row[tid] = hi - lo;
+        kseg[tid] = static_cast<const B *>(a.keys[tid]) + lo;
+        vseg[tid] = VB > 0 ? static_cast<const VT *>(a.values[tid]) + lo : nullptr;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        uint64_t base = 0;
+        uint32_t off = 0;
+        for (uint32_t t = 0; t < W; ++t) {
+            bnd[t] = off;
+            off += uint32_t(len_row[t]);
+            base += lo_row[t];
         }
-        __syncthreads();
-        if (tid == 0) {
-            uint64_t base = 0, off = 0;
-            for (uint32_t t = 0; t < W; ++t) {
-                T.bnd[t] = uint32_t(off < uint64_t(S::CAP) ? off : uint64_t(S::CAP));
-                off += len_row[t];
-                base += lo_row[t];
-            }
-            T.bnd[W] = uint32_t(off < uint64_t(S::CAP) ? off : uint64_t(S::CAP));
-            T.out_base = base;
-        }
-        __syncthreads();
-    };
-
-    B kr[ITEMS];
-    VT vr[VB > 0 ? ITEMS : 1];
-    auto load = [&](const MwTile &T) {
-        const uint32_t n = T.bnd[W];
+        bnd[W] = off;
+        out_base = base;
+    }
+    __syncthreads();
+    const uint32_t n = bnd[W];
+    // The partition bounds n by (W + G) * S <= CAP; the test only keeps a
+    // corrupt table from overrunning shared memory.
+    if (n > uint32_t(S::CAP)) return;
+    // Stage the W segments back to back.  Every load of a thread is issued
+    // before its first shared store, so ITEMS loads per thread are in flight
+    // at once (the runs may be a peer's memory, microseconds away).
+    {
+        B kr[ITEMS];
+        VT vr[VB > 0 ? ITEMS : 1];
         uint32_t t = 0;
 #pragma unroll
         for (int u = 0; u < ITEMS; ++u) {
             const uint32_t i = tid + uint32_t(u) * MW_THREADS;
             if (i < n) {
-                while (i >= T.bnd[t + 1]) ++t;
-                kr[u] = static_cast<const B *>(T.kseg[t])[i - T.bnd[t]];
-                if constexpr (VB > 0) vr[u] = static_cast<const VT *>(T.vseg[t])[i - T.bnd[t]];
+                while (i >= bnd[t + 1]) ++t;
+                kr[u] = kseg[t][i - bnd[t]];
+                if constexpr (VB > 0) vr[u] = vseg[t][i - bnd[t]];
             }
         }
-    };
-    auto store = [&](const MwTile &T) {
-        const uint32_t n = T.bnd[W];
 #pragma unroll
         for (int u = 0; u < ITEMS; ++u) {
             const uint32_t i = tid + uint32_t(u) * MW_THREADS;
@@ -226,106 +210,35 @@ __global__ void __launch_bounds__(MW_THREADS, 1) multiway_merge_kernel(MultiwayA
                 if constexpr (VB > 0) vb0[i] = vr[u];
             }
         }
-    };
-
-    uint64_t g = blockIdx.x;
-    if (g >= groups) return;
-    describe(g, tiles[0]);
-    load(tiles[0]);
-    store(tiles[0]);
+    }
     __syncthreads();
-    int cs = 0;
-    for (;;) {
-        const uint64_t gn = g + gridDim.x;
-        const bool more = gn < groups;
-        if (more) {
-            describe(gn, tiles[cs ^ 1]);
-            load(tiles[cs ^ 1]);  // in flight during the merge below
-        }
-        MwTile &T = tiles[cs];
-        uint32_t *bnd = T.bnd;
-        const uint32_t n = bnd[W];
 
-        // Pairwise rounds: segments (0,1), (2,3), ... of the current buffer
-        // merge into the other; an unpaired last segment is copied.
-        int cur = 0;
-        uint32_t segs = W;
-        while (segs > 1) {
-            const B *ik = cur ? kb1 : kb0;
-            const VT *iv = cur ? vb1 : vb0;
-            B *ok = cur ? kb0 : kb1;
-            VT *ov = cur ? vb0 : vb1;
-            const uint32_t o0 = tid * ITEMS;
-            const uint32_t oend = o0 + ITEMS < n ? o0 + ITEMS : n;
-            const uint32_t npairs = (segs + 1) >> 1;
-            // Fast path: the thread's outputs lie in one merge pair, so the merge
-            // is a fixed, unrolled ITEMS-step loop (as in the two-run merge).
-            bool done = o0 >= n;
-            if (!done) {
-                uint32_t pr = 0;
-                while (pr + 1 < npairs && bnd[2 * pr + 2] <= o0) ++pr;
-                const uint32_t sa = 2 * pr;
-                const uint32_t a0 = bnd[sa], a1 = bnd[sa + 1];
-                const uint32_t b1 = sa + 1 < segs ? bnd[sa + 2] : a1;
-                if (oend <= b1 && b1 > a1) {
-                    const uint32_t la = a1 - a0, lb = b1 - a1;
-                    const B *ta = ik + a0;
-                    const B *tb = ik + a1;
-                    const uint32_t diag = o0 - a0;
-                    uint32_t lo = diag > lb ? diag - lb : 0, hi = diag < la ? diag : la;
-                    while (lo < hi) {
-                        const uint32_t mid = (lo + hi) >> 1;
-                        if (mw_image(ta[mid], xf) <= mw_image(tb[diag - 1 - mid], xf))
-                            lo = mid + 1;
-                        else
-                            hi = mid;
-                    }
-                    uint32_t ia = lo, ib = diag - lo;
-                    uint64_t ima = ia < la ? mw_image(ta[ia], xf) : 0;
-                    uint64_t imb = ib < lb ? mw_image(tb[ib], xf) : 0;
-#pragma unroll
-                    for (int k = 0; k < ITEMS; ++k) {
-                        const bool take_a = ib >= lb || (ia < la && ima <= imb);
-                        const uint32_t src = take_a ? a0 + ia : a1 + ib;
-                        if (o0 + k < oend) {
-                            ok[o0 + k] = ik[src];
-                            if constexpr (VB > 0) ov[o0 + k] = iv[src];
-                        }
-                        if (take_a) {
-                            ++ia;
-                            if (ia < la) ima = mw_image(ta[ia], xf);
-                        } else {
-                            ++ib;
-                            if (ib < lb) imb = mw_image(tb[ib], xf);
-                        }
-                    }
-                    done = true;
-                }
-            }
-            // General path: outputs that cross a pair boundary, or a lone
-            // segment's copy.
-            uint32_t o = done ? oend : o0;
-            while (o < oend) {
-                // the pair (segments 2pr and 2pr + 1) holding output position o;
-                // a lone last segment is a pair without a right side
-                uint32_t pr = 0;
-                while (pr + 1 < npairs && bnd[2 * pr + 2] <= o) ++pr;
-                const uint32_t sa = 2 * pr;
-                const uint32_t a0 = bnd[sa];
-                const uint32_t a1 = bnd[sa + 1];
-                const uint32_t b1 = sa + 1 < segs ? bnd[sa + 2] : a1;
+    // Pairwise rounds: segments (0,1), (2,3), ... of the current buffer merge
+    // into the other; an unpaired last segment is copied.
+    int cur = 0;
+    uint32_t segs = W;
+    while (segs > 1) {
+        const B *ik = cur ? kb1 : kb0;
+        const VT *iv = cur ? vb1 : vb0;
+        B *ok = cur ? kb0 : kb1;
+        VT *ov = cur ? vb0 : vb1;
+        const uint32_t o0 = tid * ITEMS;
+        const uint32_t oend = o0 + ITEMS < n ? o0 + ITEMS : n;
+        const uint32_t npairs = (segs + 1) >> 1;
+        // Fast path: the thread's outputs lie in one merge pair, so the merge
+        // is a fixed, unrolled ITEMS-step loop (as in the two-run merge).
+        bool done = o0 >= n;
+        if (!done) {
+            uint32_t pr = 0;
+            while (pr + 1 < npairs && bnd[2 * pr + 2] <= o0) ++pr;
+            const uint32_t sa = 2 * pr;
+            const uint32_t a0 = bnd[sa], a1 = bnd[sa + 1];
+            const uint32_t b1 = sa + 1 < segs ? bnd[sa + 2] : a1;
+            if (oend <= b1 && b1 > a1) {
                 const uint32_t la = a1 - a0, lb = b1 - a1;
-                const uint32_t stop = oend < b1 ? oend : b1;
-                if (lb == 0) {  // unpaired segment: copy
-                    for (; o < stop; ++o) {
-                        ok[o] = ik[o];
-                        if constexpr (VB > 0) ov[o] = iv[o];
-                    }
-                    continue;
-                }
                 const B *ta = ik + a0;
                 const B *tb = ik + a1;
-                const uint32_t diag = o - a0;
+                const uint32_t diag = o0 - a0;
                 uint32_t lo = diag > lb ? diag - lb : 0, hi = diag < la ? diag : la;
                 while (lo < hi) {
                     const uint32_t mid = (lo + hi) >> 1;
@@ -337,11 +250,14 @@ __global__ void __launch_bounds__(MW_THREADS, 1) multiway_merge_kernel(MultiwayA
                 uint32_t ia = lo, ib = diag - lo;
                 uint64_t ima = ia < la ? mw_image(ta[ia], xf) : 0;
                 uint64_t imb = ib < lb ? mw_image(tb[ib], xf) : 0;
-                for (; o < stop; ++o) {
+#pragma unroll
+                for (int k = 0; k < ITEMS; ++k) {
                     const bool take_a = ib >= lb || (ia < la && ima <= imb);
                     const uint32_t src = take_a ? a0 + ia : a1 + ib;
-                    ok[o] = ik[src];
-                    if constexpr (VB > 0) ov[o] = iv[src];
+                    if (o0 + k < oend) {
+                        ok[o0 + k] = ik[src];
+                        if constexpr (VB > 0) ov[o0 + k] = iv[src];
+                    }
                     if (take_a) {
                         ++ia;
                         if (ia < la) ima = mw_image(ta[ia], xf);
@@ -350,32 +266,76 @@ __global__ void __launch_bounds__(MW_THREADS, 1) multiway_merge_kernel(MultiwayA
                         if (ib < lb) imb = mw_image(tb[ib], xf);
                     }
                 }
+                done = true;
             }
-            __syncthreads();
-            // merged pair p spans the old segments 2p and 2p + 1
-            const uint32_t nsegs = (segs + 1) / 2;
-            if (tid == 0) {
-                for (uint32_t p = 1; p <= nsegs; ++p) bnd[p] = bnd[2 * p < segs ? 2 * p : segs];
+        }
+        // General path: outputs that cross a pair boundary, or a lone
+        // segment's copy.
+        uint32_t o = done ? oend : o0;
+        while (o < oend) {
+            // the pair (segments 2pr and 2pr + 1) holding output position o;
+            // a lone last segment is a pair without a right side
+            uint32_t pr = 0;
+            while (pr + 1 < npairs && bnd[2 * pr + 2] <= o) ++pr;
+            const uint32_t sa = 2 * pr;
+            const uint32_t a0 = bnd[sa];
+            const uint32_t a1 = bnd[sa + 1];
+            const uint32_t b1 = sa + 1 < segs ? bnd[sa + 2] : a1;
+            const uint32_t la = a1 - a0, lb = b1 - a1;
+            const uint32_t stop = oend < b1 ? oend : b1;
+            if (lb == 0) {  // unpaired segment: copy
+                for (; o < stop; ++o) {
+                    ok[o] = ik[o];
+                    if constexpr (VB > 0) ov[o] = iv[o];
+                }
+                continue;
             }
-            __syncthreads();
-            segs = nsegs;
-            cur ^= 1;
+            const B *ta = ik + a0;
+            const B *tb = ik + a1;
+            const uint32_t diag = o - a0;
+            uint32_t lo = diag > lb ? diag - lb : 0, hi = diag < la ? diag : la;
+            while (lo < hi) {
+                const uint32_t mid = (lo + hi) >> 1;
+                if (mw_image(ta[mid], xf) <= mw_image(tb[diag - 1 - mid], xf))
+                    lo = mid + 1;
+                else
+                    hi = mid;
+            }
+            uint32_t ia = lo, ib = diag - lo;
+            uint64_t ima = ia < la ? mw_image(ta[ia], xf) : 0;
+            uint64_t imb = ib < lb ? mw_image(tb[ib], xf) : 0;
+            for (; o < stop; ++o) {
+                const bool take_a = ib >= lb || (ia < la && ima <= imb);
+                const uint32_t src = take_a ? a0 + ia : a1 + ib;
+                ok[o] = ik[src];
+                if constexpr (VB > 0) ov[o] = iv[src];
+                if (take_a) {
+                    ++ia;
+                    if (ia < la) ima = mw_image(ta[ia], xf);
+                } else {
+                    ++ib;
+                    if (ib < lb) imb = mw_image(tb[ib], xf);
+                }
+            }
         }
-
-        B *outk = static_cast<B *>(a.out_keys) + T.out_base;
-        VT *outv = VB > 0 ? static_cast<VT *>(a.out_values) + T.out_base : nullptr;
-        const B *fk = cur ? kb1 : kb0;
-        const VT *fv = cur ? vb1 : vb0;
-        for (uint32_t i = tid; i < n; i += MW_THREADS) {
-            outk[i] = fk[i];
-            if constexpr (VB > 0) outv[i] = fv[i];
-        }
-        __syncthreads();  // both buffers are free again
-        if (!more) break;
-        store(tiles[cs ^ 1]);
         __syncthreads();
-        cs ^= 1;
-        g = gn;
+        // merged pair p spans the old segments 2p and 2p + 1
+        const uint32_t nsegs = (segs + 1) / 2;
+        if (tid == 0) {
+            for (uint32_t p = 1; p <= nsegs; ++p) bnd[p] = bnd[2 * p < segs ? 2 * p : segs];
+        }
+        __syncthreads();
+        segs = nsegs;
+        cur ^= 1;
+    }
+
+    B *outk = static_cast<B *>(a.out_keys) + out_base;
+    VT *outv = VB > 0 ? static_cast<VT *>(a.out_values) + out_base : nullptr;
+    const B *fk = cur ? kb1 : kb0;
+    const VT *fv = cur ? vb1 : vb0;
+    for (uint32_t i = tid; i < n; i += MW_THREADS) {
+        outk[i] = fk[i];
+        if constexpr (VB > 0) outv[i] = fv[i];
     }
 }
 
@@ -400,18 +360,7 @@ cudaError_t multiway_t(MultiwayArgs &a, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     const uint64_t groups = (a.pivots + a.group - 1) / a.group;
     if (groups == 0) return cudaSuccess;
-    // Persistent grid: every CTA that fits at once, each taking tiles
-    // blockIdx.x, + gridDim.x, ...
-    int dev = 0, sms = 0, per_sm = 0;
-    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
-        return e;
-    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, MW_THREADS, S::BYTES)) !=
-        cudaSuccess)
-        return e;
-    const uint64_t resident = uint64_t(sms) * uint64_t(per_sm > 0 ? per_sm : 1);
-    const uint64_t grid = groups < resident ? groups : resident;
-    k<<<dim3(uint32_t(grid)), MW_THREADS, S::BYTES, s>>>(a);
+    k<<<dim3(uint32_t(groups)), MW_THREADS, S::BYTES, s>>>(a);
     return cudaGetLastError();
 }
 
