@@ -385,6 +385,68 @@ rsort_status rsort_rows_lexicographic(size_t words, void *d_rows, void *d_payloa
                                       size_t scratch_bytes, rsort_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * DeviceMergeSort by a comparator program.
+ *
+ * rccl-cub's merge sort (rccl-cub/src/dispatch.rs:170-193, 1113-1146) and
+ * Thrust's sort_by lowering (rccl-thrust/src/backend.rs:39-63) take any
+ * `Fn(&K, &K) -> Ordering` closure over any DeviceCopy record.  The closures
+ * the reference's own callers pass are key projections chained with
+ * then_with and optionally reversed:
+ *   |l, r| (l & 1).cmp(&(r & 1)).then_with(|| l.cmp(r))  rccl-thrust/examples/sort.rs:101
+ *   |l, r| (l / 10).cmp(&(r / 10))                        rccl-thrust/examples/sort.rs:111
+ *   |l, r| r.cmp(l)                                       rccl-thrust/examples/sort.rs:133
+ *   |l, r| l.key.cmp(&r.key) on a struct                  rccl-thrust/examples/set_operations_tests.rs:143-151
+ *   sort_by_key(|k| k & 0x00ff_ffff)                      rccl-cub/examples/device_ordering_benchmark.rs:162
+ * A comparator program states such a closure as data: `nterms` terms, most
+ * significant first; two records compare by the first term whose projected
+ * values differ.  Term t reads the field of type t.type at byte offset
+ * t.offset of the record, applies t.projection with t.operand (in the
+ * field's type, with Rust's integer semantics), and compares the results by
+ * t.order (rsort_order_t: floats by partial_cmp with -0.0 == +0.0, or by
+ * total_cmp; DESCENDING reverses the term).  nterms == 0 compares every
+ * record equal.
+ *   RSORT_PROJ_IDENTITY  v                   any type
+ *   RSORT_PROJ_AND       v & operand         integers
+ *   RSORT_PROJ_SHR       v >> operand        integers (arithmetic for signed),
+ *                                            0 <= operand < width
+ *   RSORT_PROJ_DIV       v / operand         integers, truncating; operand != 0,
+ *                                            and != -1 for signed types
+ *   RSORT_PROJ_REM       v % operand         integers, the dividend's sign;
+ *                                            same operand rules as DIV
+ * The sort is stable (equal records keep their input order), so its result
+ * is the comparator sort's.  It runs on the stable radix path: the terms'
+ * significant bits are packed into 64-bit keys, least significant group
+ * first, each group one stable (key, index) sort; then the records and the
+ * optional values (value_bytes each, 0 = none) are permuted in place.
+ * Fields may sit at any byte offset.  d_scratch:
+ * rsort_sort_by_scratch_bytes(record_bytes, value_bytes, n) bytes, 256-byte
+ * aligned; n must fit a 32-bit permutation; at most RSORT_MAX_TERMS terms.
+ * ------------------------------------------------------------------------- */
+#define RSORT_MAX_TERMS 16
+
+typedef enum {
+    RSORT_PROJ_IDENTITY = 0,
+    RSORT_PROJ_AND = 1,
+    RSORT_PROJ_SHR = 2,
+    RSORT_PROJ_DIV = 3,
+    RSORT_PROJ_REM = 4
+} rsort_projection_t;
+
+typedef struct {
+    uint32_t offset;               /* byte offset of the field in the record */
+    int32_t type;                  /* rsort_key_t of the field */
+    int32_t projection;            /* rsort_projection_t */
+    int32_t order;                 /* rsort_order_t */
+    int64_t operand;               /* mask, shift or divisor (the field's bits
+                                      for unsigned 64-bit masks) */
+} rsort_compare_term;
+
+size_t rsort_sort_by_scratch_bytes(size_t record_bytes, size_t value_bytes, size_t n);
+rsort_status rsort_sort_by(const rsort_compare_term *terms, size_t nterms, void *d_records,
+                           size_t record_bytes, void *d_values, size_t value_bytes, size_t n,
+                           void *d_scratch, size_t scratch_bytes, rsort_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Bucket exchange over NVLink peer memory (no reference counterpart).
  *
  * Replaces step 5 above (the NCCL all-to-all): every rank exports its sorted

@@ -74,11 +74,25 @@ EXPORTED_SYMBOLS = (
     "rsort_dist_pairs_rank",
     "rsort_multiway_scratch_bytes",
     "rsort_merge_multiway",
+    "rsort_sort_by_scratch_bytes",
+    "rsort_sort_by",
 )
 
 # rsort_exchange_t
 RSORT_EXCHANGE_NCCL = 0
 RSORT_EXCHANGE_PEER = 1
+
+
+# rsort_projection_t and the comparator-program limit
+RSORT_PROJ_IDENTITY, RSORT_PROJ_AND, RSORT_PROJ_SHR, RSORT_PROJ_DIV, RSORT_PROJ_REM = range(5)
+RSORT_MAX_TERMS = 16
+
+
+class CompareTerm(ctypes.Structure):
+    """rsort_compare_term"""
+    _fields_ = [("offset", ctypes.c_uint32), ("type", ctypes.c_int32),
+                ("projection", ctypes.c_int32), ("order", ctypes.c_int32),
+                ("operand", ctypes.c_int64)]
 
 
 class Controls(ctypes.Structure):
@@ -170,6 +184,10 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.rsort_rows_scratch_bytes.restype = sz
     lib.rsort_rows_lexicographic.argtypes = [sz, vp, vp, sz, sz, vp, sz, vp]
     lib.rsort_rows_lexicographic.restype = i
+    lib.rsort_sort_by_scratch_bytes.argtypes = [sz, sz, sz]
+    lib.rsort_sort_by_scratch_bytes.restype = sz
+    lib.rsort_sort_by.argtypes = [ctypes.POINTER(CompareTerm), sz, vp, sz, vp, sz, sz, vp, sz, vp]
+    lib.rsort_sort_by.restype = i
     lib.rsort_segmented_scratch_bytes.argtypes = [i, sz, sz, sz]
     lib.rsort_segmented_scratch_bytes.restype = sz
     lib.rsort_segmented_sort.argtypes = [i, i, vp, vp, vp, vp, sz, sz, sz, vp, vp, u, u, vp, sz,

@@ -929,6 +929,231 @@ rsort_status rsort_rows_lexicographic(size_t words, void *d_rows, void *d_payloa
     return e == cudaSuccess ? RSORT_OK : cuda_fail(e, "record sort permutation");
 }
 
+// ---------------------------------------------------------------------------
+// Comparator-program sort: DeviceMergeSort by a chain of projected-field
+// comparisons (rccl-cub/src/dispatch.rs:170-193, 1113-1146 with the closures
+// of rccl-thrust/examples/sort.rs:101-113), on the stable radix path.
+// ---------------------------------------------------------------------------
+namespace {
+
+struct SortByLayout {
+    size_t keys, keys_alt, perm, perm_alt, bins, lookback, counters, records, values, total;
+    rsort_controls c, c32, c64;  // region sizes; the exact counts of each key width
+};
+
+rsort_status sort_by_layout(size_t record_bytes, size_t value_bytes, size_t n, SortByLayout *L) {
+    // The groups sort 32- or 64-bit keys with 4-byte indices: controls for
+    // the larger of the two shapes serve both.
+    rsort_controls c64{}, c32{};
+    rsort_status st = rsort_controls_query(RSORT_U64, 4, n, &c64);
+    if (st == RSORT_OK) st = rsort_controls_query(RSORT_U32, 4, n, &c32);
+    if (st != RSORT_OK) return st;
+    const rsort_controls c{std::max(c64.bins, c32.bins), std::max(c64.lookback, c32.lookback),
+                           std::max(c64.counters, c32.counters)};
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = off;
+        off = align256(off + bytes);
+        return at;
+    };
+    L->keys = take(8 * n);
+    L->keys_alt = take(8 * n);
+    L->perm = take(4 * n);
+    L->perm_alt = take(4 * n);
+    L->bins = take(8 * c.bins);
+    L->lookback = take(4 * c.lookback);
+    L->counters = take(4 * c.counters);
+    L->records = take(record_bytes * n);
+    L->values = take(value_bytes * n);
+    L->total = off;
+    L->c = c;
+    L->c32 = c32;
+    L->c64 = c64;
+    return RSORT_OK;
+}
+
+unsigned bit_length(uint64_t v) { return v ? 64u - unsigned(__builtin_clzll(v)) : 0u; }
+
+// Checks one term and fills its device form, including the window of order
+// image bits that can differ between records (width 0: the term compares
+// every record equal).
+rsort_status prepare_term(const rsort_compare_term &t, size_t record_bytes, uintptr_t records,
+                          CompareTerm *out) {
+    const rsort_key_t key = rsort_key_t(t.type);
+    if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "comparator term type");
+    if (!order_ok(rsort_order_t(t.order))) return fail(RSORT_BAD_ARGUMENT, "comparator term order");
+    const unsigned bytes = unsigned(key_bytes(key)), W = 8 * bytes;
+    if (size_t(t.offset) + bytes > record_bytes)
+        return fail(RSORT_BAD_ARGUMENT, "comparator term field (offset + width <= record_bytes)",
+                    record_bytes, size_t(t.offset) + bytes);
+    const int kind0 = key_kind(key);
+    const int kind = kind0 == KIND_FLOAT && order_total(rsort_order_t(t.order)) ? KIND_FLOAT_TOTAL
+                                                                               : kind0;
+    const int proj = t.projection;
+    if (proj < RSORT_PROJ_IDENTITY || proj > RSORT_PROJ_REM)
+        return fail(RSORT_BAD_ARGUMENT, "comparator term projection");
+    if (kind0 == KIND_FLOAT && proj != RSORT_PROJ_IDENTITY)
+        return fail(RSORT_BAD_ARGUMENT, "comparator term projection (floats: identity only)");
+    const uint64_t wmask = W == 64 ? ~uint64_t(0) : (uint64_t(1) << W) - 1;
+    const int64_t smin = W == 64 ? INT64_MIN : -(int64_t(1) << (W - 1));
+    const int64_t smax = W == 64 ? INT64_MAX : (int64_t(1) << (W - 1)) - 1;
+    const bool is_signed = kind0 == KIND_SINT;
+    // The operand must be a value of the field's type (a 64-bit unsigned
+    // operand is passed as its bits).
+    const bool representable = is_signed ? (t.operand >= smin && t.operand <= smax)
+                                          : (W == 64 || (t.operand >= 0 && uint64_t(t.operand) <= wmask));
+    unsigned lo = 0, width = W;
+    const uint64_t op = uint64_t(t.operand) & wmask;
+    switch (proj) {
+        case RSORT_PROJ_AND:
+            if (!representable) return fail(RSORT_BAD_ARGUMENT, "comparator term mask");
+            // Without the sign bit the masked value is non-negative and the
+            // signed image's sign bit is constant: only the mask bits vary.
+            if (!is_signed || !(op >> (W - 1))) {
+                if (op == 0) {
+                    width = 0;
+                } else {
+                    lo = unsigned(__builtin_ctzll(op));
+                    width = bit_length(op) - lo;
+                }
+            }
+            break;
+        case RSORT_PROJ_SHR:
+            if (t.operand < 0 || uint64_t(t.operand) >= W)
+                return fail(RSORT_BAD_ARGUMENT, "comparator term shift (0 <= shift < width)", W,
+                            size_t(t.operand));
+            if (!is_signed) width = W - unsigned(t.operand);
+            break;
+        case RSORT_PROJ_DIV:
+        case RSORT_PROJ_REM:
+            if (!representable || op == 0 || (is_signed && t.operand == -1))
+                return fail(RSORT_BAD_ARGUMENT, "comparator term divisor (non-zero; not -1 for signed)");
+            if (!is_signed) width = proj == RSORT_PROJ_DIV ? bit_length(wmask / op) : bit_length(op - 1);
+            break;
+        default: break;
+    }
+    const bool aligned = records % bytes == 0 && record_bytes % bytes == 0 && t.offset % bytes == 0;
+    *out = CompareTerm{t.offset,
+                       uint8_t(bytes),
+                       uint8_t(kind),
+                       uint8_t(proj),
+                       uint8_t(order_desc(rsort_order_t(t.order)) ? 1 : 0),
+                       uint8_t(aligned ? 1 : 0),
+                       uint8_t(lo),
+                       uint8_t(width),
+                       int64_t(op)};
+    if (is_signed) out->operand = t.operand;
+    return RSORT_OK;
+}
+
+}  // namespace
+
+size_t rsort_sort_by_scratch_bytes(size_t record_bytes, size_t value_bytes, size_t n) {
+    SortByLayout L{};
+    return sort_by_layout(record_bytes, value_bytes, n, &L) == RSORT_OK ? L.total : 0;
+}
+
+rsort_status rsort_sort_by(const rsort_compare_term *terms, size_t nterms, void *d_records,
+                           size_t record_bytes, void *d_values, size_t value_bytes, size_t n,
+                           void *d_scratch, size_t scratch_bytes, rsort_stream_t stream) {
+    if (nterms > RSORT_MAX_TERMS)
+        return fail(RSORT_BAD_ARGUMENT, "comparator terms (at most RSORT_MAX_TERMS)", RSORT_MAX_TERMS,
+                    nterms);
+    if (nterms && !terms) return fail(RSORT_BAD_ARGUMENT, "null comparator terms");
+    if (record_bytes == 0) return fail(RSORT_BAD_ARGUMENT, "record width");
+    if (n > 0xffffffffull) return fail(RSORT_SIZE_OVERFLOW, "record count (32-bit permutation)");
+    if (n > 1 && (!d_records || (value_bytes && !d_values))) return fail(RSORT_BAD_ARGUMENT, "null buffer");
+    // Groups of terms packed into one key, least significant group first;
+    // each group's terms most significant first.
+    std::vector<CompareGroup> groups;
+    {
+        std::vector<CompareTerm> kept;
+        for (size_t i = 0; i < nterms; ++i) {
+            CompareTerm ct{};
+            rsort_status st = prepare_term(terms[i], record_bytes,
+                                           reinterpret_cast<uintptr_t>(d_records), &ct);
+            if (st != RSORT_OK) return st;
+            if (ct.width) kept.push_back(ct);
+        }
+        for (size_t i = kept.size(); i-- > 0;) {
+            if (groups.empty() || groups.back().total_bits + kept[i].width > 64 ||
+                groups.back().nterms == COMPARE_GROUP_MAX)
+                groups.push_back(CompareGroup{});
+            CompareGroup &g = groups.back();
+            // prepend: terms run most significant first within a group
+            for (uint32_t k = g.nterms; k > 0; --k) g.term[k] = g.term[k - 1];
+            g.term[0] = kept[i];
+            ++g.nterms;
+            g.total_bits += kept[i].width;
+        }
+    }
+    if (n <= 1 || groups.empty()) return RSORT_OK;
+    SortByLayout L{};
+    rsort_status st = sort_by_layout(record_bytes, value_bytes, n, &L);
+    if (st != RSORT_OK) return st;
+    if (!d_scratch || scratch_bytes < L.total)
+        return fail(RSORT_WORKSPACE_TOO_SMALL, "sort_by scratch", L.total, scratch_bytes);
+    DeviceInfo dev;
+    st = device_info(&dev);
+    if (st != RSORT_OK) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    char *base = static_cast<char *>(d_scratch);
+    void *keys = base + L.keys;
+    void *keys_alt = base + L.keys_alt;
+    uint32_t *perm = reinterpret_cast<uint32_t *>(base + L.perm);
+    uint32_t *perm_alt = reinterpret_cast<uint32_t *>(base + L.perm_alt);
+    // One set of control regions, sized for the larger shape; each group's
+    // sort gets the exact counts of its key width.
+    auto controls = [&](const rsort_controls &k) {
+        return Controls{reinterpret_cast<uint64_t *>(base + L.bins), k.bins,
+                        reinterpret_cast<int32_t *>(base + L.lookback), k.lookback,
+                        reinterpret_cast<int32_t *>(base + L.counters), k.counters};
+    };
+    const Controls c32 = controls(L.c32), c64 = controls(L.c64);
+    const uint8_t *records = static_cast<const uint8_t *>(d_records);
+    cudaError_t e = L.c.counters ? cudaMemsetAsync(c64.counters, 0, 4 * L.c.counters, s)
+                                 : cudaSuccess;
+    if (e != cudaSuccess) return cuda_fail(e, "sort_by counters");
+    {
+        LaunchScope scope(RSORT_KERNEL_RECORDS, s);
+        e = launch_iota(perm, n, dev.sm_count, s);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "sort_by permutation");
+    // LSD over the groups; every group is a stable sort of (key, index).
+    for (size_t gi = 0; gi < groups.size(); ++gi) {
+        const CompareGroup &g = groups[gi];
+        {
+            LaunchScope scope(RSORT_KERNEL_RECORDS, s);
+            e = launch_compare_keys(records, record_bytes, gi == 0 ? nullptr : perm, n, g, keys,
+                                    dev.sm_count, s);
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "sort_by keys");
+        int cur_first = 1;
+        const bool narrow = g.total_bits <= 32;
+        st = sort_buffer(narrow ? RSORT_U32 : RSORT_U64, 0, keys, keys_alt, perm, perm_alt, 4, n, 0,
+                         g.total_bits, &cur_first, narrow ? c32 : c64, s);
+        if (st != RSORT_OK) return st;
+        if (!cur_first) std::swap(perm, perm_alt);
+    }
+    // Apply the permutation to the records and values.
+    char *rec_tmp = base + L.records;
+    {
+        LaunchScope scope(RSORT_KERNEL_RECORDS, s);
+        e = launch_permute(d_records, perm, n, record_bytes, rec_tmp, dev.sm_count, s);
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d_records, rec_tmp, record_bytes * n, cudaMemcpyDeviceToDevice, s);
+    if (e == cudaSuccess && value_bytes) {
+        char *val_tmp = base + L.values;
+        {
+            LaunchScope scope(RSORT_KERNEL_RECORDS, s);
+            e = launch_permute(d_values, perm, n, value_bytes, val_tmp, dev.sm_count, s);
+        }
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(d_values, val_tmp, value_bytes * n, cudaMemcpyDeviceToDevice, s);
+    }
+    return e == cudaSuccess ? RSORT_OK : cuda_fail(e, "sort_by permutation");
+}
+
 // One word per merge tile plus one, and one more per pair of a batched round
 // (rsort_merge_runs / rsort_merge_segments launch up to MERGE_MAX_PAIRS pair
 // merges at once, each with its own closing word).

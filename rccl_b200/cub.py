@@ -17,7 +17,7 @@ from typing import Optional, Tuple
 
 import torch
 
-from . import _lib
+from . import _lib, compare
 from .errors import (BadArgument, DeviceAlgorithmError, LengthMismatch, raise_for)
 
 KEY_TYPES = {
@@ -397,7 +397,8 @@ def order_code(order) -> int:
     if callable(order):
         raise NotImplementedError(
             "a comparator closure is device code; pass one of rccl_b200.cub.Order "
-            "(ASCENDING, DESCENDING, TOTAL_ASCENDING, TOTAL_DESCENDING)")
+            "(ASCENDING, DESCENDING, TOTAL_ASCENDING, TOTAL_DESCENDING) or a comparator "
+            "program (rccl_b200.compare.Key / Comparator)")
     raise BadArgument(f"unknown sort order {order!r}")
 
 
@@ -414,9 +415,38 @@ def device_merge_sort_pairs_workspace(launch: Launch, key_dtype: torch.dtype, va
     return device_radix_sort_pairs_workspace(launch, key_dtype, value_dtype, n)
 
 
-def device_merge_sort_keys(launch: Launch, keys: torch.Tensor,
-                           workspace: DeviceRadixSortKeysWorkspace, order) -> None:
-    """Stable in-place sort by a named order (dispatch.rs:170-193)."""
+@dataclass
+class DeviceMergeSortByWorkspace:
+    """Scratch of a sort by a comparator program (rsort_sort_by_scratch_bytes):
+    packed term keys, the index permutation, radix controls and the staging
+    of records and values."""
+    scratch: torch.Tensor
+
+
+def device_merge_sort_by_workspace(launch: Launch, records: torch.Tensor,
+                                   values: Optional[torch.Tensor] = None
+                                   ) -> DeviceMergeSortByWorkspace:
+    """Workspace of device_merge_sort_keys / _pairs with a comparator program
+    (rccl_b200.compare) over these records (and values)."""
+    nbytes = compare.scratch_bytes(records, values)
+    return DeviceMergeSortByWorkspace(
+        torch.empty(max(nbytes, 1), dtype=torch.uint8, device=launch.device))
+
+
+def _sort_by_program(launch: Launch, keys, values, workspace, order) -> None:
+    if not isinstance(workspace, DeviceMergeSortByWorkspace):
+        raise BadArgument("a comparator program needs device_merge_sort_by_workspace")
+    launch.check(keys, values, workspace.scratch)
+    compare.sort_by(keys, values, order, workspace.scratch, launch.handle)
+
+
+def device_merge_sort_keys(launch: Launch, keys: torch.Tensor, workspace, order) -> None:
+    """Stable in-place sort by a named order or a comparator program
+    (dispatch.rs:170-193).  Records of a comparator program are the rows of
+    `keys` (any dtype and row shape)."""
+    if compare.is_program(order):
+        _sort_by_program(launch, keys, None, workspace, order)
+        return
     code = order_code(order)
     launch.check(keys, workspace.scratch_keys)
     raise_for(_lib.lib().rsort_merge_sort_keys(
@@ -425,8 +455,12 @@ def device_merge_sort_keys(launch: Launch, keys: torch.Tensor,
 
 
 def device_merge_sort_pairs(launch: Launch, keys: torch.Tensor, values: torch.Tensor,
-                            workspace: DeviceRadixSortPairsWorkspace, order) -> None:
-    """Stable in-place key/value sort by a named order (dispatch.rs:1113-1146)."""
+                            workspace, order) -> None:
+    """Stable in-place key/value sort by a named order or a comparator program
+    (dispatch.rs:1113-1146)."""
+    if compare.is_program(order):
+        _sort_by_program(launch, keys, values, workspace, order)
+        return
     code = order_code(order)
     launch.check(keys, values, workspace.scratch_keys, workspace.scratch_values)
     if values.shape[0] != keys.numel():

@@ -15,7 +15,7 @@ from typing import Optional
 
 import torch
 
-from . import _lib
+from . import _lib, compare
 from .cub import (KEY_TYPES, BadArgument, ContextMismatch, Launch, Order, Program as CubProgram,
                   controls_counts, key_code, order_code, value_bytes_of)
 from .errors import LengthMismatch, UnsupportedTarget, raise_for
@@ -146,16 +146,34 @@ def sort_unstable(execution: Execution, keys: torch.Tensor) -> None:
     _radix_sort(execution, keys)
 
 
+def _sort_by_program(execution: Execution, records: torch.Tensor,
+                     values: Optional[torch.Tensor], order) -> None:
+    """sort_by with a comparator program: one temporary block (the
+    rsort_sort_by scratch), the sort, release, synchronization -- the same
+    lowering shape as backend.rs:39-63."""
+    launch = execution.launch
+    launch.check(records, values)
+    tmp = _Temporary(launch.device, [compare.scratch_bytes(records, values)], [256])
+    compare.sort_by(records, values, order, tmp.block, launch.handle)
+    del tmp
+    execution.synchronize()
+
+
 def sort_by(execution: Execution, keys: torch.Tensor, order) -> None:
-    """Stable in-place sort by a named order (DeviceSortExt::sort_by,
+    """Stable in-place sort by a comparator (DeviceSortExt::sort_by,
     ordering.rs:78-87; the reference lowers it to DeviceMergeSort).  `order`
-    is a rccl_b200.cub.Order: the comparator closure itself is device code."""
-    _radix_sort(execution, keys, order_code(order))
+    is a named order (rccl_b200.cub.Order) or a comparator program
+    (rccl_b200.compare.Key / Comparator) over the rows of `keys`: the closure
+    itself is device code."""
+    if compare.is_program(order):
+        _sort_by_program(execution, keys, None, order)
+    else:
+        _radix_sort(execution, keys, order_code(order))
 
 
 def sort_unstable_by(execution: Execution, keys: torch.Tensor, order) -> None:
     """DeviceSortExt::sort_unstable_by (ordering.rs:58-68); stable here."""
-    _radix_sort(execution, keys, order_code(order))
+    sort_by(execution, keys, order)
 
 
 class KeyValueRangeMut:
@@ -172,11 +190,15 @@ class KeyValueRangeMut:
         _radix_sort_pairs(execution, self.keys, self.values)
 
     def sort_by(self, execution: Execution, order) -> None:
-        """DeviceKeyValueSortExt::sort_by (ordering.rs:170-181) by a named order."""
-        _radix_sort_pairs(execution, self.keys, self.values, order_code(order))
+        """DeviceKeyValueSortExt::sort_by (ordering.rs:170-181) by a named
+        order or a comparator program over the key rows."""
+        if compare.is_program(order):
+            _sort_by_program(execution, self.keys, self.values, order)
+        else:
+            _radix_sort_pairs(execution, self.keys, self.values, order_code(order))
 
     def sort_unstable_by(self, execution: Execution, order) -> None:
-        _radix_sort_pairs(execution, self.keys, self.values, order_code(order))
+        self.sort_by(execution, order)
 
 
 class RangeError(ValueError):
@@ -186,9 +208,11 @@ class RangeError(ValueError):
 
 
 def with_values(keys: torch.Tensor, values: torch.Tensor) -> KeyValueRangeMut:
-    """DeviceViewMut::with_values (range.rs:158-163, length check :320-334)."""
-    if keys.numel() != values.shape[0]:
-        raise RangeError(keys.numel(), values.shape[0])
+    """DeviceViewMut::with_values (range.rs:158-163, length check :320-334).
+    Keys may be record rows (an (n, ...) tensor) for a comparator program."""
+    n = keys.shape[0] if keys.dim() else keys.numel()
+    if n != values.shape[0]:
+        raise RangeError(n, values.shape[0])
     return KeyValueRangeMut(keys, values)
 
 

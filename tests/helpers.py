@@ -70,3 +70,45 @@ def order_image(keys: np.ndarray, descending: bool = False) -> np.ndarray:
     if keys.dtype.kind == "f":
         o = np.where(o == sign - ut(1), sign, o)
     return o.astype(np.uint64)
+
+
+def load_compare_cases():
+    """The reference's comparator-sort golden cases (make_compare_golden.py)."""
+    with open(os.path.join(GOLDEN, "compare_probes.json")) as fh:
+        meta = json.load(fh)
+    arrays = np.load(os.path.join(GOLDEN, "compare_probes.npz"))
+    out = []
+    for m in meta:
+        name = m["name"]
+        case = dict(m)
+        case["records"] = arrays[f"{name}__records"]
+        case["expected"] = arrays[f"{name}__expected"]
+        if m["has_values"]:
+            case["values"] = arrays[f"{name}__values"]
+            case["expected_values"] = arrays[f"{name}__expected_values"]
+        out.append(case)
+    return out
+
+
+def oracle_terms(terms):
+    """Golden-case term dicts -> oracle.compare_oracle.Term."""
+    from oracle.compare_oracle import Term
+    return [Term(np.dtype(t["dtype"]), t["offset"], t["projection"], t["operand"],
+                 t["descending"], t["total"]) for t in terms]
+
+
+def program_of(terms):
+    """Golden-case term dicts -> rccl_b200.compare.Comparator."""
+    import torch
+    from rccl_b200 import compare
+    keys = []
+    for t in terms:
+        k = compare.Key(torch.from_numpy(np.zeros(0, np.dtype(t["dtype"]))).dtype, t["offset"])
+        if t["projection"] != "identity":
+            k = getattr(k, {"and": "and_"}.get(t["projection"], t["projection"]))(t["operand"])
+        if t["descending"]:
+            k = k.reverse()
+        if t["total"]:
+            k = k.total()
+        keys.append(k)
+    return compare.Comparator(tuple(keys))
