@@ -509,7 +509,11 @@ void rsort_launch_count_reset(void);
 /* Kernel ids reported by rsort_profile_read. */
 enum { RSORT_KERNEL_INIT = 0, RSORT_KERNEL_HISTOGRAM = 1, RSORT_KERNEL_ONESWEEP = 2,
        RSORT_KERNEL_SINGLE_TILE = 3, RSORT_KERNEL_DIST = 4, RSORT_KERNEL_MERGE = 5,
-       RSORT_KERNEL_GATHER = 6, RSORT_KERNEL_RECORDS = 7 };
+       RSORT_KERNEL_GATHER = 6, RSORT_KERNEL_RECORDS = 7,
+       /* the uniform-step form of a pass after the first (4- and 8-byte keys):
+        * it sorts passes where runs of equal keys are expected and exits at
+        * once elsewhere, so a pass costs this launch plus the onesweep launch */
+       RSORT_KERNEL_ONESWEEP_RUNS = 8 };
 
 /* Benchmark instrumentation (no reference counterpart): while enabled, every
  * kernel launch of the calling host thread is bracketed by CUDA events on its

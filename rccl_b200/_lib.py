@@ -30,7 +30,7 @@ RSORT_BAD_ARGUMENT = 8
 
 # kernel ids of rsort_profile_read
 KERNEL_NAMES = {0: "init", 1: "histogram", 2: "onesweep", 3: "single_tile", 4: "dist",
-                5: "merge", 6: "gather", 7: "records"}
+                5: "merge", 6: "gather", 7: "records", 8: "onesweep_runs"}
 IPC_HANDLE_BYTES = 64
 GATHER_MAX_SEGMENTS = 64
 

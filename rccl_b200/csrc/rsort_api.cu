@@ -294,6 +294,7 @@ rsort_status sort_buffer(rsort_key_t key, int descending, void *kf, void *ks, vo
     h.kind = kind;
     h.desc = descending ? 1 : 0;
     h.vector_ok = (reinterpret_cast<uintptr_t>(kin) & 15) == 0;
+    h.hot = c.counters + CTR_HOT_FLAGS;
     {
         LaunchScope scope(RSORT_KERNEL_HISTOGRAM, stream);
         e = launch_histogram(kb, h, dev.sm_count, stream);
@@ -322,6 +323,16 @@ rsort_status sort_buffer(rsort_key_t key, int descending, void *kf, void *ks, vo
         a.first = p == 0;
         a.last = p + 1 == passes;
         a.tag = p + 1;
+        a.hot = c.counters + CTR_HOT_FLAGS;
+        a.pass = p;
+        // Passes after the first: the RANK_RUNS form goes first and takes
+        // the pass when it and the pass before are hot (long runs of equal
+        // keys); otherwise it exits and the plain pass claims every tile.
+        if (p > 0 && kb >= 4 && n >= RUNS_MIN_ITEMS) {
+            LaunchScope scope(RSORT_KERNEL_ONESWEEP_RUNS, stream);
+            e = launch_onesweep_runs(kb, int(vb), a, tiles, stream);
+            if (e != cudaSuccess) return cuda_fail(e, "onesweep launch");
+        }
         {
             LaunchScope scope(RSORT_KERNEL_ONESWEEP, stream);
             e = launch_onesweep(kb, int(vb), a, tiles, stream);

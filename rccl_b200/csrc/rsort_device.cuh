@@ -342,9 +342,25 @@ __device__ __forceinline__ uint32_t match_digit(uint32_t d, bool check_valid) {
 // and a three-sync single-array form were all measured slower on sm_100.)
 constexpr int RANK_MASK_SETS = 3;
 
+// Uniform steps: after the first pass, equal keys lie next to each other, so
+// with long runs of equal keys (duplicate-heavy inputs) most warp steps hold
+// one digit in all 32 lanes, and their 32 atomicOrs to one mask word
+// serialize.  In RANK_RUNS mode a shuffle and a vote find each such step,
+// whose peer mask is then the whole warp: no mask word is touched.
+constexpr int RANK_PLAIN = 0;
+constexpr int RANK_RUNS = 1;
+
+// A pass whose digit histogram has one digit holding at least 1/HOT_SHARE
+// of the keys (short of all of them) is "hot".  A pass after the first runs
+// the RANK_RUNS kernel when it and the pass before are both hot: that is
+// where long runs of equal keys come from.  Measured on B200 (2^30 u32
+// keys, 90% Zipf(1.1) + 10% one constant, all passes hot).
+constexpr uint32_t HOT_SHARE = 16;
+
 // rank[j] = digit << 16 | rank of item j among the warp's items of its digit.
 // ALL_VALID: no padding items (full tile), so no per-item validity tests.
-template <int ITEMS, bool ALL_VALID, typename DigitAt>
+// MODE: RANK_PLAIN or RANK_RUNS (ALL_VALID only).
+template <int ITEMS, bool ALL_VALID, int MODE = RANK_PLAIN, typename DigitAt>
 __device__ __forceinline__ void warp_rank_items_or3(DigitAt digit_at, uint32_t (&rank)[ITEMS],
                                                     uint32_t *whist, uint32_t *wmask) {
     const uint32_t lane = threadIdx.x & 31;
@@ -356,20 +372,25 @@ __device__ __forceinline__ void warp_rank_items_or3(DigitAt digit_at, uint32_t (
         uint32_t *m = wmask + (j % 3) * RADIX;
         const uint32_t d = digit_at(j);
         const bool valid = ALL_VALID || d < RADIX;
-        if (valid) atomicOr(&m[d], bit);
+        bool uniform = false;  // RANK_RUNS: every lane of the step holds digit d
+        if constexpr (MODE == RANK_RUNS) {
+            static_assert(ALL_VALID, "uniform steps are found in full tiles only");
+            uniform = __all_sync(0xffffffffu, d == __shfl_sync(0xffffffffu, d, 0));
+        }
+        if (valid && !uniform) atomicOr(&m[d], bit);
         // Orders this item's ORs before the reads below, the previous item's
         // reads before its clear below, and the previous item's whist update
         // before this item's whist read.
         __syncwarp();
         if (prev_leader) wmask[((j + 2) % 3) * RADIX + prev_d] = 0u;
-        const uint32_t peers = valid ? m[d] : 0u;
+        const uint32_t peers = uniform ? 0xffffffffu : valid ? m[d] : 0u;
         const uint32_t leader = 31 - __clz(peers);
         const bool is_leader = valid && lane == leader;
         // One shared atomic per group: it returns the running count and
         // advances it (measured 2-5% faster per pass than a load and a store).
         uint32_t got = 0;
         if (is_leader) got = atomicAdd(&whist[d], __popc(peers));
-        prev_leader = is_leader;
+        prev_leader = is_leader && !uniform;  // a uniform step set no mask word
         prev_d = d;
         // Packed (digit << 16 | rank): the rank within the warp is below
         // 32 * ITEMS < 2^16, and the scatter reads the digit back from here.

@@ -189,12 +189,16 @@ __global__ void __launch_bounds__(HIST_THREADS, 1) histogram_kernel(HistArgs a) 
     __syncthreads();
     if (!is_last) return;
     __threadfence();
+    uint32_t hot = 0;  // bit p: pass p is hot
     for (uint32_t p = 0; p < a.passes; ++p) {
         uint64_t v = 0;
         if (tid < RADIX) v = __ldcg(&a.bins[p * RADIX + tid]);
+        if (__syncthreads_or(tid < RADIX && v != a.n && v * HOT_SHARE >= a.n) && p < 32)
+            hot |= 1u << p;
         const uint64_t ex = block_exclusive_scan_256_u64(v, warp_sums);
         if (tid < RADIX) a.bins[p * RADIX + tid] = ex;
     }
+    if (a.hot && tid == 0) *a.hot = int(hot);
 }
 
 // ---------------------------------------------------------------------------
@@ -243,6 +247,9 @@ struct OnesweepSmem {
 template <bool V> struct BoolTag {
     static constexpr bool value = V;
 };
+template <int V> struct IntTag {
+    static constexpr int value = V;
+};
 
 // PERSIST: a persistent grid whose CTAs claim tiles until none are left and
 // load the next tile while writing out the current one (measured faster for
@@ -250,8 +257,15 @@ template <bool V> struct BoolTag {
 // tiles are larger).  The per-tile body is compiled twice, for full tiles
 // (no per-item bounds tests, fully unrolled write-out) and for the last,
 // partial tile.
-template <typename B, int VB, int ITEMS, int KIND, bool PERSIST>
+// RUNS: the RANK_RUNS form (persistent grids only): it sorts the pass only
+// when this pass and the one before are hot, else it returns at once.
+template <typename B, int VB, int ITEMS, int KIND, bool PERSIST, bool RUNS = false>
 __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_kernel(PassArgs a) {
+    if constexpr (RUNS) {
+        static_assert(PERSIST, "the RANK_RUNS form runs on a persistent grid");
+        const int hot = a.hot && a.pass >= 1 && a.pass < 32 ? *a.hot : 0;
+        if (!((hot >> a.pass) & (hot >> (a.pass - 1)) & 1)) return;
+    }
     using L = OnesweepSmem<B, VB, ITEMS>;
     using VT = typename ValueType<VB>::type;
     constexpr int THREADS = L::THREADS, WARPS = L::WARPS, TILE = L::TILE;
@@ -371,8 +385,10 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
 
     // One tile: rank, totals and scan, scatter into shared memory, look-back,
     // write-out.  Returns the next tile id.
-    auto tile_body = [&](auto full_tag, const int64_t tile, const uint32_t count) -> int64_t {
+    auto tile_body = [&](auto full_tag, auto mode_tag, const int64_t tile,
+                         const uint32_t count) -> int64_t {
         constexpr bool FULL = decltype(full_tag)::value;
+        constexpr int MODE = decltype(mode_tag)::value;
         auto live = [&](int j) { return FULL || seg + j * 32 + lane < count; };
 
         // 1. Stable warp multi-split rank over warp-private histograms.
@@ -387,8 +403,8 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
 #ifdef RSORT_RANK_BALLOT
         warp_rank_items<ITEMS>(digit_at, rank, whist + warp * RADIX, !FULL);
 #else
-        warp_rank_items_or3<ITEMS, FULL>(digit_at, rank, whist + warp * WHIST_WORDS,
-                                         wmask + warp * RANK_MASK_SETS * RADIX);
+        warp_rank_items_or3<ITEMS, FULL, MODE>(digit_at, rank, whist + warp * WHIST_WORDS,
+                                               wmask + warp * RANK_MASK_SETS * RADIX);
 #endif
         __syncthreads();
         const int64_t next = PERSIST ? int64_t(ctl[2]) : tiles;
@@ -499,8 +515,12 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
         if constexpr (PERSIST) {
             if (tid == 0) ctl[2] = atomicAdd(a.tile_counter, 1);
         }
-        const int64_t next = count == uint32_t(TILE) ? tile_body(BoolTag<true>{}, tile, count)
-                                                     : tile_body(BoolTag<false>{}, tile, count);
+        // Full tiles of the RUNS form take the uniform-step rank (a per-tile
+        // choice between the two ranks measured slower on skewed passes).
+        const int64_t next =
+            count == uint32_t(TILE)
+                ? tile_body(BoolTag<true>{}, IntTag<(RUNS ? RANK_RUNS : RANK_PLAIN)>{}, tile, count)
+                : tile_body(BoolTag<false>{}, IntTag<RANK_PLAIN>{}, tile, count);
         if (!PERSIST || next >= tiles) break;
 
         // The staging area aliases the mask arrays: every write-out read is
@@ -644,15 +664,16 @@ cudaError_t ensure_smem(Kernel k, size_t bytes) {
     return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
 }
 
-template <typename B, int VB>
+// RUNS: the RANK_RUNS form, always on a persistent grid.
+template <typename B, int VB, bool RUNS = false>
 cudaError_t onesweep_t(const PassArgs &a, uint64_t tiles, cudaStream_t s) {
     constexpr int ITEMS = onesweep_items(int(sizeof(B)), VB);
     using L = OnesweepSmem<B, VB, ITEMS>;
-    constexpr bool P = sizeof(B) == 8;
-    auto k = a.kind == KIND_FLOAT         ? onesweep_kernel<B, VB, ITEMS, KIND_FLOAT, P>
-             : a.kind == KIND_FLOAT_TOTAL ? onesweep_kernel<B, VB, ITEMS, KIND_FLOAT_TOTAL, P>
-             : a.kind == KIND_SINT        ? onesweep_kernel<B, VB, ITEMS, KIND_SINT, P>
-                                          : onesweep_kernel<B, VB, ITEMS, KIND_UINT, P>;
+    constexpr bool P = RUNS || sizeof(B) == 8;
+    auto k = a.kind == KIND_FLOAT         ? onesweep_kernel<B, VB, ITEMS, KIND_FLOAT, P, RUNS>
+             : a.kind == KIND_FLOAT_TOTAL ? onesweep_kernel<B, VB, ITEMS, KIND_FLOAT_TOTAL, P, RUNS>
+             : a.kind == KIND_SINT        ? onesweep_kernel<B, VB, ITEMS, KIND_SINT, P, RUNS>
+                                          : onesweep_kernel<B, VB, ITEMS, KIND_UINT, P, RUNS>;
     cudaError_t e = ensure_smem(k, L::BYTES);
     if (e != cudaSuccess) return e;
     if (!P) {
@@ -682,15 +703,15 @@ cudaError_t single_t(const SingleArgs &a, cudaStream_t s) {
     return cudaGetLastError();
 }
 
-template <typename B>
+template <typename B, bool RUNS = false>
 cudaError_t onesweep_vb(int vb, const PassArgs &a, uint64_t tiles, cudaStream_t s) {
     switch (vb) {
-        case 0: return onesweep_t<B, 0>(a, tiles, s);
-        case 1: return onesweep_t<B, 1>(a, tiles, s);
-        case 2: return onesweep_t<B, 2>(a, tiles, s);
-        case 4: return onesweep_t<B, 4>(a, tiles, s);
-        case 8: return onesweep_t<B, 8>(a, tiles, s);
-        case 16: return onesweep_t<B, 16>(a, tiles, s);
+        case 0: return onesweep_t<B, 0, RUNS>(a, tiles, s);
+        case 1: return onesweep_t<B, 1, RUNS>(a, tiles, s);
+        case 2: return onesweep_t<B, 2, RUNS>(a, tiles, s);
+        case 4: return onesweep_t<B, 4, RUNS>(a, tiles, s);
+        case 8: return onesweep_t<B, 8, RUNS>(a, tiles, s);
+        case 16: return onesweep_t<B, 16, RUNS>(a, tiles, s);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -764,6 +785,15 @@ cudaError_t launch_onesweep(int key_bytes, int value_bytes, const PassArgs &a, u
         case 4: return onesweep_vb<uint32_t>(value_bytes, a, tiles, stream);
         case 8: return onesweep_vb<uint64_t>(value_bytes, a, tiles, stream);
         default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_onesweep_runs(int key_bytes, int value_bytes, const PassArgs &a,
+                                 uint64_t tiles, cudaStream_t stream) {
+    switch (key_bytes) {
+        case 4: return onesweep_vb<uint32_t, true>(value_bytes, a, tiles, stream);
+        case 8: return onesweep_vb<uint64_t, true>(value_bytes, a, tiles, stream);
+        default: return cudaSuccess;  // 1- and 2-byte keys: the plain pass only
     }
 }
 

@@ -1,6 +1,8 @@
 """GPU parity: the CUDA path (through the C ABI, via the rccl_cub / rccl_thrust
 mirrors) against the reference's golden vectors and against the CPU oracle on
 seeded inputs.  Integer, byte and index work: every comparison is bit-exact."""
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -11,6 +13,8 @@ from rccl_b200 import cub, thrust
 from rccl_b200.errors import InvalidBitRange
 
 pytestmark = pytest.mark.gpu
+
+THREADS = os.cpu_count() or 1
 
 CASES = load_cases()
 TORCH_OF = {"uint32": torch.uint32, "int32": torch.int32, "float32": torch.float32,
@@ -275,3 +279,46 @@ def test_non_default_stream(launch):
     cub.device_radix_sort_keys(l2, t, ws)
     s.synchronize()
     assert np.array_equal(to_host(t), np.sort(k))
+
+
+# The uniform-step form of a pass (RANK_RUNS) takes passes after the first
+# when the pass and the one before each have a digit holding 1/16 of the
+# keys, in sorts of at least 2^25 items.
+RUNS_MIN_ITEMS = 1 << 25
+
+
+@pytest.mark.parametrize("kname", KEY_NAMES)
+@pytest.mark.parametrize("with_values", [False, True])
+def test_runs_of_equal_keys_parity(launch, kname, with_values):
+    """Duplicate-heavy input at 2^25 + 4321 items: six heavy values holding
+    30% down to 6.5% of the keys over a uniform rest, so every pass is hot
+    and, after the first, sorted runs of equal keys fill whole warp steps.
+    Checked bit-exactly against the oracle; value indices check stability."""
+    rng = np.random.default_rng(23)
+    dt = NP_OF[kname]
+    n = RUNS_MIN_ITEMS + 4321
+    k = gen_keys(rng, dt, n, "uniform")
+    heavy = gen_keys(rng, dt, 6, "uniform")
+    which = np.searchsorted(np.cumsum([0.30, 0.15, 0.08, 0.07, 0.065, 0.065]), rng.random(n))
+    for h in range(heavy.size):
+        k[which == h] = heavy[h]
+    v = np.arange(n, dtype=np.uint32) if with_values else None
+    desc = with_values  # both directions across the parametrization
+    gk, gv, cur_first = gpu_sort(launch, k, v, desc)
+    ok, ov, swaps, st = O.radix_sort(k, v, desc, threads=THREADS)
+    assert st == 0
+    assert np.array_equal(bits(gk), bits(ok))
+    if v is not None:
+        assert np.array_equal(gv, ov)
+    assert cur_first == (swaps % 2 == 0)
+
+
+def test_runs_form_below_threshold_parity(launch):
+    """The same kind of input below 2^25 items (plain passes only)."""
+    rng = np.random.default_rng(29)
+    n = (1 << 20) + 77
+    k = rng.integers(0, 2**32, n, dtype=np.uint64).astype(np.uint32)
+    k[rng.random(n) < 0.4] = 123456789
+    v = np.arange(n, dtype=np.uint32)
+    for desc in (False, True):
+        check_against_oracle(launch, k, v, desc)
