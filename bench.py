@@ -421,14 +421,17 @@ def read_profile(L, cap: int):
 
 def roofline_of(workload: Workload, per_kernel, sort_ms: float | None):
     """Roofline of the dominant kernel (the onesweep pass): algorithmic bytes
-    per launch over its mean CUDA-event launch time, against the measured
+    per pass over the mean CUDA-event time of a pass, against the measured
     HBM peak; with `sort_ms`, also the whole sort's byte model over the sort
-    time."""
+    time.  A pass after the first is two launches -- the uniform-step form
+    (onesweep_runs), which sorts passes with runs of equal keys and exits at
+    once elsewhere, then the onesweep kernel, which exits at once where the
+    first sorted the pass -- so a pass's time is the sum of both."""
     peak, peak_kind = measured_peak()
     osw = per_kernel.get("onesweep", [])
     if not osw:
         return None
-    avg_s = statistics.mean(osw) / 1e3
+    avg_s = (sum(osw) + sum(per_kernel.get("onesweep_runs", []))) / len(osw) / 1e3
     achieved = workload.bytes_per_pass / avg_s / 1e9
     out = {"bound": "hbm", "kernel": "onesweep", "achieved": achieved, "peak": peak,
            "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
