@@ -78,6 +78,22 @@ def splitmix64(idx, seed: int):
     return z ^ _lsr(z, 31)
 
 
+def multiset_hash(keys):
+    """Order-independent hash of a key tensor: the wrapping int64 sum of a
+    splitmix64 mix of each key's bits.  Equal for any permutation of the same
+    keys, so a sort's output must reproduce its input's value (a checksum of
+    checksums across ranks when summed over them)."""
+    import torch
+    w = keys.view(torch.int32 if keys.element_size() == 4 else torch.int64)
+    total = torch.zeros((), dtype=torch.int64, device=keys.device)
+    for a in range(0, w.numel(), CHUNK):
+        bits = w[a:a + CHUNK].to(torch.int64)
+        if keys.element_size() == 4:
+            bits &= 0xFFFFFFFF
+        total += splitmix64(bits, 0x5EED).sum()
+    return total
+
+
 def uniform01(h):
     """Uniform float64 in (0, 1] from a 64-bit word."""
     import torch
@@ -1017,6 +1033,12 @@ def run_dist(args, workload: Workload):
         restore()
         out = global_sort(keys, values)
         del out
+    in_hash = None
+    if values is None:
+        # keys-only: the multiset of all ranks' input keys, for the output check
+        restore()
+        in_hash = multiset_hash(keys)
+        dist.all_reduce(in_hash)
     torch.cuda.synchronize()
     dist.barrier()
 
@@ -1064,6 +1086,11 @@ def run_dist(args, workload: Workload):
     else:
         img = image_i64(ok_k, np.dtype(workload.key).kind, workload.desc)
         ok = bool(torch.all(img[1:] >= img[:-1])) if img.numel() else True
+        del img
+        # the parts of all ranks together are a permutation of all inputs
+        out_hash = multiset_hash(ok_k)
+        dist.all_reduce(out_hash)
+        ok &= bool(out_hash == in_hash)
     kind = np.dtype(workload.key).kind
     if ok_k.numel():
         img_ends = image_i64(torch.cat([ok_k[:1], ok_k[-1:]]), kind, workload.desc)
@@ -1198,7 +1225,9 @@ def run_dist(args, workload: Workload):
             "output_checked": bool(oks.item() == 1 and bound_ok and total_out == n_total),
             "check": ("bit-exact per rank (keys regenerated from value indices, order, "
                       "stability), every global index exactly once over all ranks, rank "
-                      "boundaries ordered"),
+                      "boundaries ordered" if vd is not None else
+                      "keys-only: each rank's part in order, rank boundaries ordered, and the "
+                      "multiset hash of all output parts equal to that of all inputs"),
             "out_per_rank": counts,
             "e2e": e2e if e2e is not None else {"unavailable": e2e_skip},
         }
