@@ -32,23 +32,35 @@ __global__ void init_kernel(uint64_t *bins, uint32_t nbins, int *counters, uint3
 // look-back words for the whole sort, and the last CTA to finish turns the
 // digit counts into global exclusive digit offsets (one scan per pass).
 //
-// Counter layout: one column of counters per lane (32 columns for 32-bit
-// keys, 16 for 64-bit keys), counter (pass, digit, column) at word
-// (pass * 256 + digit) * COLS + column.  Lane l of every warp adds into
-// column l % COLS, so the 32 lanes of one shared atomic hit 32 different
-// banks (64-bit keys: at most 2 lanes per bank) whatever the digits are: the
-// count runs at the shared-atomic issue rate, also on skewed inputs where a
-// single-copy histogram serializes on one address.  The 128 KB of counters
-// take the shared memory of one 1024-thread CTA per SM.
+// Counter layout: one column of counters per lane, counter (row, digit,
+// column) at word (row * 256 + digit) * 32 + column.  Lane l of every warp
+// adds into column l, so the 32 lanes of one shared atomic hit 32 different
+// banks whatever the digits are: the count runs at the shared-atomic issue
+// rate, also on skewed inputs where a single-copy histogram serializes on one
+// address.  Keys of up to 4 bytes have one row of 32-bit counters per pass.
+// 8-byte keys (8 passes) would need 256 KB that way; they keep 16-bit
+// counters instead, passes p and p + 4 in the low and high halves of row
+// p % 4's words, and every CTA adds its counts into the bins and clears them
+// before any counter can reach 2^16 (HistShape::FLUSH_KEYS).  (With 16
+// columns of 32-bit counters, lanes l and l + 16 shared a bank, so every
+// atomic took two shared-memory cycles: 0.59 ms for config 2's 2^28 u64 keys
+// against 0.33 ms of HBM time.)  The 128 KB of counters take the shared
+// memory of one 1024-thread CTA per SM.
 // ---------------------------------------------------------------------------
 constexpr int HIST_THREADS = 1024;
 constexpr int HIST_UNROLL = 4;
 
 template <typename B> struct HistShape {
     static constexpr int MAX_PASSES = int(sizeof(B));  // 8-bit digits
-    static constexpr int COLS = sizeof(B) <= 4 ? 32 : 16;
-    static constexpr size_t WORDS = size_t(MAX_PASSES) * RADIX * COLS;
+    static constexpr bool PACKED = sizeof(B) == 8;
+    static constexpr int COLS = 32;
+    static constexpr int ROWS = PACKED ? 4 : MAX_PASSES;
+    static constexpr size_t WORDS = size_t(ROWS) * RADIX * COLS;
     static constexpr size_t BYTES = WORDS * 4;
+    // PACKED: keys one thread may count between two flushes.  A column is
+    // shared by lane l of the CTA's 32 warps, and each key adds one to one
+    // counter of every pass, so a counter stays at most 32 * FLUSH_KEYS.
+    static constexpr uint32_t FLUSH_KEYS = 65535 / (HIST_THREADS / 32);
 };
 
 __device__ __forceinline__ uint64_t block_exclusive_scan_256_u64(uint64_t v, uint64_t *warp_sums) {
@@ -93,7 +105,10 @@ __device__ __forceinline__ void hist_count(B raw, B dmask, uint32_t passes, uint
             const uint32_t mask = uint32_t(p) + 1 == passes ? last_mask : 0xffu;
             d = uint32_t(o >> (begin_bit + 8 * p)) & mask;
         }
-        atomicAdd(hc + (p * RADIX + d) * S::COLS, 1u);
+        if constexpr (S::PACKED)
+            atomicAdd(hc + ((p & 3) * RADIX + d) * S::COLS, 1u << (16 * (p >> 2)));
+        else
+            atomicAdd(hc + (p * RADIX + d) * S::COLS, 1u);
     }
 }
 
@@ -132,6 +147,36 @@ __global__ void __launch_bounds__(HIST_THREADS, 1) histogram_kernel(HistArgs a) 
     const uint64_t stride = uint64_t(gridDim.x) * HIST_THREADS;
     const uint64_t gtid = uint64_t(blockIdx.x) * HIST_THREADS + tid;
     const B *keys = static_cast<const B *>(a.keys);
+
+    // Column sums into the global bins; each lane starts at a different
+    // column so the reads of a warp spread over the banks.
+    auto add_columns = [&]() {
+        for (uint32_t i = tid; i < passes * RADIX; i += HIST_THREADS) {
+            const uint32_t p = i / RADIX, d = i % RADIX;
+            const uint32_t row = S::PACKED ? (p & 3) * RADIX + d : i;
+            const uint32_t sh = S::PACKED ? 16 * (p >> 2) : 0;
+            uint32_t c = 0;
+#pragma unroll 8
+            for (int k = 0; k < S::COLS; ++k) {
+                const uint32_t w = h[row * S::COLS + ((k + lane) % S::COLS)];
+                c += S::PACKED ? (w >> sh) & 0xffffu : w;
+            }
+            if (c) atomicAdd(reinterpret_cast<unsigned long long *>(&a.bins[i]),
+                             static_cast<unsigned long long>(c));
+        }
+    };
+    // PACKED: between two chunks of the key range, every CTA adds its counts
+    // into the bins and clears them.  The chunk loops below are uniform over
+    // the grid, so every thread of a CTA reaches these barriers together.
+    auto flush = [&]() {
+        __syncthreads();
+        add_columns();
+        __syncthreads();
+        uint4 *h4 = reinterpret_cast<uint4 *>(h);
+        for (uint32_t i = tid; i < S::WORDS / 4; i += HIST_THREADS) h4[i] = make_uint4(0, 0, 0, 0);
+        __syncthreads();
+    };
+
     uint64_t scalar_begin = 0;
     if (a.vector_ok) {
         // HIST_UNROLL independent 16-byte loads per thread are in flight
@@ -140,7 +185,8 @@ __global__ void __launch_bounds__(HIST_THREADS, 1) histogram_kernel(HistArgs a) 
         constexpr int PER = 16 / sizeof(B);
         const uint64_t nvec = a.n / PER;
         const uint4 *kv = reinterpret_cast<const uint4 *>(keys);
-        for (uint64_t i = gtid; i < nvec; i += stride * HIST_UNROLL) {
+        const uint64_t step = stride * HIST_UNROLL;
+        auto count_block = [&](uint64_t i) {
             uint4 v[HIST_UNROLL];
 #pragma unroll
             for (int u = 0; u < HIST_UNROLL; ++u) {
@@ -168,21 +214,37 @@ __global__ void __launch_bounds__(HIST_THREADS, 1) histogram_kernel(HistArgs a) 
                     count((uint64_t(v[u].w) << 32) | v[u].z);
                 }
             }
+        };
+        if constexpr (S::PACKED) {
+            // One iteration of a thread counts HIST_UNROLL * PER keys from the
+            // grid's step-aligned block of `step` vectors, so a chunk of whole
+            // blocks holds every load its iterations issue.
+            const uint64_t chunk = step * (S::FLUSH_KEYS / (HIST_UNROLL * PER));
+            for (uint64_t c0 = 0; c0 < nvec; c0 += chunk) {
+                const uint64_t c1 = nvec - c0 < chunk ? nvec : c0 + chunk;
+                for (uint64_t i = c0 + gtid; i < c1; i += step) count_block(i);
+                if (c1 < nvec) flush();
+            }
+        } else {
+            for (uint64_t i = gtid; i < nvec; i += step) count_block(i);
         }
         scalar_begin = nvec * PER;
     }
-    for (uint64_t i = scalar_begin + gtid; i < a.n; i += stride) count(keys[i]);
-    __syncthreads();
-
-    // Column sums; each lane starts at a different column so the reads of a
-    // warp spread over the banks.
-    for (uint32_t i = tid; i < passes * RADIX; i += HIST_THREADS) {
-        uint32_t c = 0;
-#pragma unroll 8
-        for (int k = 0; k < S::COLS; ++k) c += h[i * S::COLS + ((k + lane) % S::COLS)];
-        if (c) atomicAdd(reinterpret_cast<unsigned long long *>(&a.bins[i]),
-                         static_cast<unsigned long long>(c));
+    // Keys the vector loop did not take (an unaligned input, or the last
+    // PER - 1 keys): one key per thread and iteration; PACKED counters in
+    // chunks of FLUSH_KEYS iterations.
+    if constexpr (S::PACKED) {
+        const uint64_t chunk = stride * S::FLUSH_KEYS;
+        for (uint64_t c0 = scalar_begin; c0 < a.n; c0 += chunk) {
+            const uint64_t c1 = a.n - c0 < chunk ? a.n : c0 + chunk;
+            for (uint64_t i = c0 + gtid; i < c1; i += stride) count(keys[i]);
+            if (c1 < a.n) flush();
+        }
+    } else {
+        for (uint64_t i = scalar_begin + gtid; i < a.n; i += stride) count(keys[i]);
     }
+    __syncthreads();
+    add_columns();
     __threadfence();
     __syncthreads();
     if (tid == 0) is_last = atomicAdd(a.done, 1) == int(gridDim.x) - 1;
