@@ -19,6 +19,12 @@
  *    selector change (rccl-cub/src/radix.rs:467-469).
  *  - The reference's "Policy800 one-portion maximum" length limit
  *    (rccl-cub/src/radix.rs:377-384) is deliberately lifted: offsets are 64-bit.
+ *    A sort takes at most RSORT_MAX_ITEMS items (RSORT_SIZE_OVERFLOW beyond):
+ *    the decoupled look-back counts are 48-bit and the tile counters 32-bit.
+ *  - The entry points whose scratch is one blob carved into regions
+ *    (rsort_segmented_sort, rsort_rows_lexicographic, rsort_sort_by) want it
+ *    256-byte aligned and reject other addresses with RSORT_BAD_ARGUMENT
+ *    before any device work; allocations from cudaMalloc or PyTorch are.
  */
 #ifndef RSORT_B200_H
 #define RSORT_B200_H
@@ -87,6 +93,8 @@ typedef struct {
     size_t actual;
     unsigned begin_bit, end_bit, key_bits; /* InvalidBitRange payload */
 } rsort_error_info;
+
+#define RSORT_MAX_ITEMS ((size_t)1 << 40)
 
 /* Control-region sizes for `n` items (replaces
  * rccl-cub/src/workspace.rs:68-106 device_radix_sort_*workspace_counts).

@@ -33,6 +33,7 @@ KERNEL_NAMES = {0: "init", 1: "histogram", 2: "onesweep", 3: "single_tile", 4: "
                 5: "merge", 6: "gather", 7: "records", 8: "onesweep_runs"}
 IPC_HANDLE_BYTES = 64
 GATHER_MAX_SEGMENTS = 64
+MAX_ITEMS = 1 << 40  # RSORT_MAX_ITEMS
 
 EXPORTED_SYMBOLS = (
     "rsort_controls_query",

@@ -113,6 +113,25 @@ rsort_status cuda_fail(cudaError_t e, const char *role) {
     return fail(RSORT_CUDA_ERROR, role);
 }
 
+// A scratch blob is carved into 256-byte aligned regions (8-byte keys,
+// 16-byte aligned look-back words), so the blob must start on 256 bytes.
+// Checked before any launch: a misaligned region would fault the kernels.
+rsort_status check_blob(const void *d_scratch, const char *role) {
+    if ((reinterpret_cast<uintptr_t>(d_scratch) & 255) != 0)
+        return fail(RSORT_BAD_ARGUMENT, role, 256, reinterpret_cast<uintptr_t>(d_scratch) & 255);
+    return RSORT_OK;
+}
+
+// bytes_per_item * n bytes of a scratch region, or false past the radix item
+// limit or past 2^56 bytes (far beyond any device, and small enough that a
+// layout's sum of regions cannot wrap a size_t).
+bool region_bytes(size_t bytes_per_item, size_t n, size_t *out) {
+    constexpr size_t kMaxRegion = size_t(1) << 56;
+    if (n > RSORT_MAX_ITEMS || (bytes_per_item && n > kMaxRegion / bytes_per_item)) return false;
+    *out = bytes_per_item * n;
+    return true;
+}
+
 bool key_ok(rsort_key_t k) { return int(k) >= RSORT_U32 && int(k) <= RSORT_BF16; }
 int key_bytes(rsort_key_t k) {
     switch (k) {
@@ -240,7 +259,16 @@ rsort_status sort_buffer(rsort_key_t key, int descending, void *kf, void *ks, vo
     const unsigned passes = (end_bit - begin_bit + 7) / 8;
     // rccl-cub/src/radix.rs:467-469
     if (n == 0 || passes == 0) return RSORT_OK;
+    if (n > RSORT_MAX_ITEMS)
+        return fail(RSORT_SIZE_OVERFLOW, "radix item count (at most RSORT_MAX_ITEMS)",
+                    RSORT_MAX_ITEMS, n);
     if (!kf || !ks || (vb && (!vf || !vs))) return fail(RSORT_BAD_ARGUMENT, "null buffer");
+    {
+        rsort_status st = check_alignment(addr(kf) | addr(ks), size_t(kb), "radix keys alignment");
+        if (st == RSORT_OK)
+            st = check_alignment(addr(vf) | addr(vs), vb, "radix values alignment");
+        if (st != RSORT_OK) return st;
+    }
     const bool cur_first = *current_is_first != 0;
     void *kin = cur_first ? kf : ks;
     void *kout = cur_first ? ks : kf;
@@ -353,6 +381,9 @@ rsort_status rsort_controls_query(rsort_key_t key, size_t value_bytes, size_t n,
     if (!out) return fail(RSORT_BAD_ARGUMENT, "null output");
     if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
     if (!value_ok(value_bytes)) return fail(RSORT_BAD_ARGUMENT, "radix value width");
+    if (n > RSORT_MAX_ITEMS)
+        return fail(RSORT_SIZE_OVERFLOW, "radix item count (at most RSORT_MAX_ITEMS)",
+                    RSORT_MAX_ITEMS, n);
     const int kb = key_bytes(key);
     if (single_route(n, kb, int(value_bytes))) {
         out->bins = out->lookback = out->counters = 0;
@@ -565,6 +596,9 @@ rsort_status rsort_dist_samples(rsort_key_t key, int descending, const void *d_s
         return fail(RSORT_SIZE_OVERFLOW, "sample position");
     if (samples == 0) return RSORT_OK;
     if (!d_samples || (m && !d_sorted_keys)) return fail(RSORT_BAD_ARGUMENT, "null buffer");
+    if (check_alignment(addr(d_sorted_keys), size_t(key_bytes(key)), "sample keys alignment") ||
+        check_alignment(addr(d_samples), 8, "samples alignment (8 bytes)"))
+        return RSORT_BAD_ARGUMENT;
     DeviceInfo dev;
     rsort_status st = device_info(&dev);
     if (st != RSORT_OK) return st;
@@ -586,6 +620,8 @@ rsort_status rsort_dist_splitters(const void *d_samples, size_t total, unsigned 
         return fail(RSORT_WORKSPACE_TOO_SMALL, "splitter sample set", MAX_SPLITTER_SAMPLES, total);
     if (world == 1) return RSORT_OK;
     if (!d_samples || !d_splitters) return fail(RSORT_BAD_ARGUMENT, "null buffer");
+    if (check_alignment(addr(d_samples) | addr(d_splitters), 8, "samples alignment (8 bytes)"))
+        return RSORT_BAD_ARGUMENT;
     DeviceInfo dev;
     rsort_status st = device_info(&dev);
     if (st != RSORT_OK) return st;
@@ -606,6 +642,10 @@ rsort_status rsort_dist_bounds(rsort_key_t key, int descending, const void *d_so
     if (world < 1 || !d_bounds || (world > 1 && !d_splitters))
         return fail(RSORT_BAD_ARGUMENT, "null buffer");
     if (m >= (size_t(1) << POS_BITS)) return fail(RSORT_SIZE_OVERFLOW, "sample position");
+    if (check_alignment(addr(d_sorted_keys), size_t(key_bytes(key)), "bound keys alignment") ||
+        check_alignment(addr(d_splitters), 8, "splitters alignment (8 bytes)") ||
+        check_alignment(addr(d_bounds), 8, "bounds alignment"))
+        return RSORT_BAD_ARGUMENT;
     DeviceInfo dev;
     rsort_status st = device_info(&dev);
     if (st != RSORT_OK) return st;
@@ -696,6 +736,7 @@ struct SegLayout {
 
 rsort_status seg_layout(rsort_key_t key, size_t vb, size_t n, size_t nseg, SegLayout *L) {
     if (!key_ok(key)) return fail(RSORT_BAD_ARGUMENT, "radix key type");
+    if (nseg > 0xffffffffull) return fail(RSORT_SIZE_OVERFLOW, "segment count");
     rsort_controls c{};
     // Controls sized for a segment of all n items bound every segment.
     rsort_status st = rsort_controls_query(key, vb, n, &c);
@@ -740,11 +781,24 @@ rsort_status rsort_segmented_sort(rsort_key_t key, int descending, const void *d
     if (!d_keys_in || !d_keys_out || !d_begin_offsets || !d_end_offsets ||
         (value_bytes && (!d_values_in || !d_values_out)))
         return fail(RSORT_BAD_ARGUMENT, "null buffer");
+    {
+        rsort_status st = check_alignment(addr(d_keys_in) | addr(d_keys_out), size_t(kb),
+                                          "segmented keys alignment");
+        if (st == RSORT_OK)
+            st = check_alignment(addr(d_values_in) | addr(d_values_out), value_bytes,
+                                 "segmented values alignment");
+        if (st == RSORT_OK)
+            st = check_alignment(addr(d_begin_offsets) | addr(d_end_offsets), 8,
+                                 "segment offsets alignment");
+        if (st != RSORT_OK) return st;
+    }
     SegLayout L{};
     rsort_status st = seg_layout(key, value_bytes, n, nseg, &L);
     if (st != RSORT_OK) return st;
     if (!d_scratch || scratch_bytes < L.total)
         return fail(RSORT_WORKSPACE_TOO_SMALL, "segmented sort scratch", L.total, scratch_bytes);
+    st = check_blob(d_scratch, "segmented sort scratch alignment (256 bytes)");
+    if (st != RSORT_OK) return st;
     DeviceInfo dev;
     st = device_info(&dev);
     if (st != RSORT_OK) return st;
@@ -838,6 +892,10 @@ struct RowsLayout {
 size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
 rsort_status rows_layout(size_t words, size_t payload_bytes, size_t n, RowsLayout *L) {
+    if (words > (size_t(1) << 20)) return fail(RSORT_BAD_ARGUMENT, "record width");
+    size_t row_region = 0, payload_region = 0;
+    if (!region_bytes(4 * words, n, &row_region) || !region_bytes(payload_bytes, n, &payload_region))
+        return fail(RSORT_SIZE_OVERFLOW, "record sort scratch size");
     rsort_controls c{};
     rsort_status st = rsort_controls_query(RSORT_U64, 4, n, &c);
     if (st != RSORT_OK) return st;
@@ -854,8 +912,8 @@ rsort_status rows_layout(size_t words, size_t payload_bytes, size_t n, RowsLayou
     L->bins = take(8 * c.bins);
     L->lookback = take(4 * c.lookback);
     L->counters = take(4 * c.counters);
-    L->rows = take(4 * words * n);
-    L->payload = take(payload_bytes * n);
+    L->rows = take(row_region);
+    L->payload = take(payload_region);
     L->total = off;
     L->c = c;
     return RSORT_OK;
@@ -875,11 +933,15 @@ rsort_status rsort_rows_lexicographic(size_t words, void *d_rows, void *d_payloa
     if (n > 0xffffffffull) return fail(RSORT_SIZE_OVERFLOW, "record count (32-bit permutation)");
     if (words > (size_t(1) << 20)) return fail(RSORT_BAD_ARGUMENT, "record width");
     if (!d_rows || (payload_bytes && !d_payload)) return fail(RSORT_BAD_ARGUMENT, "null buffer");
+    if (check_alignment(addr(d_rows), 4, "record rows alignment (32-bit words)") != RSORT_OK)
+        return RSORT_BAD_ARGUMENT;
     RowsLayout L{};
     rsort_status st = rows_layout(words, payload_bytes, n, &L);
     if (st != RSORT_OK) return st;
     if (!d_scratch || scratch_bytes < L.total)
         return fail(RSORT_WORKSPACE_TOO_SMALL, "record sort scratch", L.total, scratch_bytes);
+    st = check_blob(d_scratch, "record sort scratch alignment (256 bytes)");
+    if (st != RSORT_OK) return st;
     DeviceInfo dev;
     st = device_info(&dev);
     if (st != RSORT_OK) return st;
@@ -953,6 +1015,9 @@ struct SortByLayout {
 };
 
 rsort_status sort_by_layout(size_t record_bytes, size_t value_bytes, size_t n, SortByLayout *L) {
+    size_t record_region = 0, value_region = 0;
+    if (!region_bytes(record_bytes, n, &record_region) || !region_bytes(value_bytes, n, &value_region))
+        return fail(RSORT_SIZE_OVERFLOW, "sort_by scratch size");
     // The groups sort 32- or 64-bit keys with 4-byte indices: controls for
     // the larger of the two shapes serve both.
     rsort_controls c64{}, c32{};
@@ -974,8 +1039,8 @@ rsort_status sort_by_layout(size_t record_bytes, size_t value_bytes, size_t n, S
     L->bins = take(8 * c.bins);
     L->lookback = take(4 * c.lookback);
     L->counters = take(4 * c.counters);
-    L->records = take(record_bytes * n);
-    L->values = take(value_bytes * n);
+    L->records = take(record_region);
+    L->values = take(value_region);
     L->total = off;
     L->c = c;
     L->c32 = c32;
@@ -1104,6 +1169,8 @@ rsort_status rsort_sort_by(const rsort_compare_term *terms, size_t nterms, void 
     if (st != RSORT_OK) return st;
     if (!d_scratch || scratch_bytes < L.total)
         return fail(RSORT_WORKSPACE_TOO_SMALL, "sort_by scratch", L.total, scratch_bytes);
+    st = check_blob(d_scratch, "sort_by scratch alignment (256 bytes)");
+    if (st != RSORT_OK) return st;
     DeviceInfo dev;
     st = device_info(&dev);
     if (st != RSORT_OK) return st;
@@ -1209,6 +1276,15 @@ rsort_status merge_impl(rsort_key_t key, int descending, bool total, const void 
     if (!out_keys || (na && !a_keys) || (nb && !b_keys) ||
         (value_bytes && (!out_values || (na && !a_values) || (nb && !b_values))))
         return fail(RSORT_BAD_ARGUMENT, "null buffer");
+    {
+        rsort_status st = check_alignment(addr(a_keys) | addr(b_keys) | addr(out_keys),
+                                          size_t(key_bytes(key)), "merge keys alignment");
+        if (st == RSORT_OK)
+            st = check_alignment(addr(a_values) | addr(b_values) | addr(out_values), value_bytes,
+                                 "merge values alignment");
+        if (st == RSORT_OK) st = check_alignment(addr(d_partitions), 8, "merge partitions alignment");
+        if (st != RSORT_OK) return st;
+    }
     if (merge_partition_words(na, nb) > 0x7fffffffull) return fail(RSORT_SIZE_OVERFLOW, "merge tiles");
     if (!d_partitions || npartitions < merge_partition_words(na, nb))
         return fail(RSORT_WORKSPACE_TOO_SMALL, "merge partitions", merge_partition_words(na, nb),
@@ -1293,6 +1369,12 @@ rsort_status rsort_merge_runs(rsort_key_t key, int descending, void *keys, void 
     if (runs > 1 && total > 0) {
         if (!keys || !scratch_keys || (value_bytes && (!values || !scratch_values)))
             return fail(RSORT_BAD_ARGUMENT, "null buffer");
+        rsort_status sa = check_alignment(addr(keys) | addr(scratch_keys), size_t(kb),
+                                          "merge keys alignment");
+        if (sa == RSORT_OK)
+            sa = check_alignment(addr(values) | addr(scratch_values), value_bytes,
+                                 "merge values alignment");
+        if (sa != RSORT_OK) return sa;
         DeviceInfo dev;
         rsort_status st = device_info(&dev);
         if (st != RSORT_OK) return st;
@@ -1375,6 +1457,14 @@ rsort_status rsort_merge_segments(rsort_key_t key, int descending, unsigned runs
     }
     if (off > 0) {
         if (!ok || (value_bytes && !ov)) return fail(RSORT_BAD_ARGUMENT, "null buffer");
+        uintptr_t kbits = addr(ok), vbits = addr(ov);
+        for (unsigned r = 0; r < runs; ++r) {
+            kbits |= addr(run_keys[r]);
+            if (value_bytes) vbits |= addr(run_values[r]);
+        }
+        rsort_status sa = check_alignment(kbits, size_t(kb), "merge keys alignment");
+        if (sa == RSORT_OK) sa = check_alignment(vbits, value_bytes, "merge values alignment");
+        if (sa != RSORT_OK) return sa;
         DeviceInfo dev;
         rsort_status st = device_info(&dev);
         if (st != RSORT_OK) return st;

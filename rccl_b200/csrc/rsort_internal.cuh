@@ -16,6 +16,19 @@ namespace rsort {
 rsort_status record_failure(rsort_status s, const char *role, size_t expected = 0,
                             size_t actual = 0);
 
+// The kernels load and store keys and values as whole elements, so every
+// buffer must be aligned to its element size: a misaligned address would
+// fault the kernel and leave the context unusable.  Entry points reject it
+// first.  `bits` is the OR of the buffers' addresses (null adds nothing);
+// the error's expected/actual are the alignment and the address remainder.
+inline rsort_status check_alignment(uintptr_t bits, size_t align, const char *role) {
+    if (align > 1 && (bits & (align - 1)) != 0)
+        return record_failure(RSORT_BAD_ARGUMENT, role, align, size_t(bits & (align - 1)));
+    return RSORT_OK;
+}
+
+inline uintptr_t addr(const void *p) { return reinterpret_cast<uintptr_t>(p); }
+
 // Kernel launch bookkeeping: counts the launch and, when profiling is on,
 // brackets it with CUDA events on `stream` (rsort_profile_*).
 struct LaunchScope {

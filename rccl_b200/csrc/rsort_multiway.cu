@@ -456,6 +456,18 @@ rsort_status rsort_merge_multiway(rsort_key_t key, int descending, unsigned runs
     if (total == 0) return RSORT_OK;
     if (!out_keys || (value_bytes && !out_values))
         return record_failure(RSORT_BAD_ARGUMENT, "multiway merge: null output");
+    {
+        uintptr_t kbits = rsort::addr(out_keys), vbits = rsort::addr(out_values);
+        for (unsigned t = 0; t < runs; ++t) {
+            kbits |= rsort::addr(run_keys[t]);
+            if (value_bytes) vbits |= rsort::addr(run_values[t]);
+        }
+        rsort_status st = rsort::check_alignment(kbits, size_t(key_bytes_mw(key)),
+                                                 "multiway merge: keys alignment");
+        if (st == RSORT_OK)
+            st = rsort::check_alignment(vbits, value_bytes, "multiway merge: values alignment");
+        if (st != RSORT_OK) return st;
+    }
     const size_t need = rsort_multiway_scratch_bytes(key, value_bytes, runs, total);
     if (!d_scratch || scratch_bytes < need)
         return record_failure(RSORT_WORKSPACE_TOO_SMALL, "multiway merge scratch", need,

@@ -102,3 +102,71 @@ def test_static_entry_point_errors_set_last_error():
     assert _lib.last_error().status == _lib.RSORT_BAD_ARGUMENT
     assert L.rsort_keys_static(_lib.RSORT_U32, 0, None, 100, None) == _lib.RSORT_BAD_ARGUMENT
     assert b"null" in _lib.last_error().role
+
+
+def _last_role():
+    return _lib.last_error().role or b""
+
+
+def test_misaligned_buffers_rejected_before_any_launch():
+    """Keys, values and merge inputs must be aligned to their element size:
+    the kernels move whole elements, and a misaligned address would fault the
+    GPU.  Every entry point rejects one on the host (the addresses here are
+    never dereferenced)."""
+    n = 100_000
+    c = _lib.Controls()
+    assert L.rsort_controls_query(_lib.RSORT_U64, 0, n, ctypes.byref(c)) == 0
+    st = L.rsort_keys(_lib.RSORT_U64, 0, 0x10004, 0x200000, n, n, 0x300000, c.bins, 0x400000,
+                      c.lookback, 0x500000, c.counters, None)
+    assert st == _lib.RSORT_BAD_ARGUMENT
+    err = _lib.last_error()
+    assert b"alignment" in err.role and err.expected == 8 and err.actual == 4
+    # the single-tile route checks too
+    st = L.rsort_keys(_lib.RSORT_F32, 0, 0x10002, 0x200000, 100, 100, None, 0, None, 0, None, 0,
+                      None)
+    assert st == _lib.RSORT_BAD_ARGUMENT and b"keys alignment" in _last_role()
+    assert L.rsort_controls_query(_lib.RSORT_U32, 8, n, ctypes.byref(c)) == 0
+    st = L.rsort_pairs(_lib.RSORT_U32, 0, 0x10000, 0x20004, 8, 0x200000, n, 0x300000, n, n,
+                       0x400000, c.bins, 0x500000, c.lookback, 0x600000, c.counters, None)
+    assert st == _lib.RSORT_BAD_ARGUMENT and b"values alignment" in _last_role()
+    st = L.rsort_merge(_lib.RSORT_U64, 0, 0x10004, None, 10, 0x20000, None, 10, 0x30000, None, 0,
+                       0x40000, 1000, None)
+    assert st == _lib.RSORT_BAD_ARGUMENT and b"merge keys alignment" in _last_role()
+    st = L.rsort_rows_lexicographic(3, 0x10002, None, 0, 1000, 0x100000,
+                                    L.rsort_rows_scratch_bytes(3, 0, 1000), None)
+    assert st == _lib.RSORT_BAD_ARGUMENT and b"rows alignment" in _last_role()
+    st = L.rsort_dist_samples(_lib.RSORT_U64, 0, 0x10004, 1000, 0, 4, 0x20000, None)
+    assert st == _lib.RSORT_BAD_ARGUMENT
+
+
+def test_scratch_blobs_must_be_256_byte_aligned():
+    n, nseg = 10_000, 4
+    need = L.rsort_segmented_scratch_bytes(_lib.RSORT_U32, 0, n, nseg)
+    st = L.rsort_segmented_sort(_lib.RSORT_U32, 0, 0x10000, 0x20000, None, None, 0, n, nseg,
+                                0x30000, 0x40000, 0, 32, 0x100040, need, None)
+    assert st == _lib.RSORT_BAD_ARGUMENT
+    err = _lib.last_error()
+    assert b"scratch alignment" in err.role and err.expected == 256 and err.actual == 0x40
+    need = L.rsort_rows_scratch_bytes(3, 0, 1000)
+    st = L.rsort_rows_lexicographic(3, 0x10000, None, 0, 1000, 0x100008, need, None)
+    assert st == _lib.RSORT_BAD_ARGUMENT and b"scratch alignment" in _last_role()
+    term = (_lib.CompareTerm * 1)()
+    term[0].offset, term[0].type, term[0].projection, term[0].order, term[0].operand = (
+        0, _lib.RSORT_U32, _lib.RSORT_PROJ_IDENTITY, 0, 0)
+    need = L.rsort_sort_by_scratch_bytes(8, 0, 1000)
+    st = L.rsort_sort_by(term, 1, 0x10000, 8, None, 0, 1000, 0x100010, need, None)
+    assert st == _lib.RSORT_BAD_ARGUMENT and b"scratch alignment" in _last_role()
+
+
+def test_item_count_and_scratch_size_limits():
+    c = _lib.Controls()
+    big = _lib.MAX_ITEMS + 1
+    assert L.rsort_controls_query(_lib.RSORT_U32, 0, big, ctypes.byref(c)) == (
+        _lib.RSORT_SIZE_OVERFLOW)
+    assert L.rsort_controls_query(_lib.RSORT_U32, 0, _lib.MAX_ITEMS, ctypes.byref(c)) == 0
+    st = L.rsort_keys(_lib.RSORT_U32, 0, 0x10000, 0x20000, big, big, 0x30000, 1024, 0x40000, 16,
+                      0x50000, 16, None)
+    assert st == _lib.RSORT_SIZE_OVERFLOW
+    # scratch regions that would wrap a size_t size as 0 (no valid layout)
+    assert L.rsort_sort_by_scratch_bytes(1 << 30, 0, 1 << 30) == 0
+    assert L.rsort_rows_scratch_bytes(3, 1 << 40, 1 << 20) == 0
