@@ -63,26 +63,6 @@ template <typename B> struct HistShape {
     static constexpr uint32_t FLUSH_KEYS = 65535 / (HIST_THREADS / 32);
 };
 
-__device__ __forceinline__ uint64_t block_exclusive_scan_256_u64(uint64_t v, uint64_t *warp_sums) {
-    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    uint64_t inc = v;
-    if (tid < RADIX) {
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-            uint64_t y = __shfl_up_sync(0xffffffffu, inc, off);
-            if (lane >= uint32_t(off)) inc += y;
-        }
-        if (lane == 31) warp_sums[warp] = inc;
-    }
-    __syncthreads();
-    uint64_t prefix = 0;
-#pragma unroll
-    for (int w = 0; w < RADIX / 32; ++w)
-        if (uint32_t(w) < warp) prefix += warp_sums[w];
-    __syncthreads();
-    return prefix + inc - v;
-}
-
 // Counts one key into every pass's digit counters (column already applied to
 // `hc`).  FULL: the bit window is the whole key, so every shift is a
 // compile-time constant.
@@ -116,7 +96,6 @@ template <typename B, int KIND, bool FULL>
 __global__ void __launch_bounds__(HIST_THREADS, 1) histogram_kernel(HistArgs a) {
     using S = HistShape<B>;
     extern __shared__ __align__(16) uint32_t h[];
-    __shared__ uint64_t warp_sums[8];
     __shared__ int is_last;
     const uint32_t tid = threadIdx.x, lane = tid & 31;
     {
@@ -251,14 +230,32 @@ __global__ void __launch_bounds__(HIST_THREADS, 1) histogram_kernel(HistArgs a) 
     __syncthreads();
     if (!is_last) return;
     __threadfence();
-    uint32_t hot = 0;  // bit p: pass p is hot
-    for (uint32_t p = 0; p < a.passes; ++p) {
-        uint64_t v = 0;
-        if (tid < RADIX) v = __ldcg(&a.bins[p * RADIX + tid]);
-        if (__syncthreads_or(tid < RADIX && v != a.n && v * HOT_SHARE >= a.n) && p < 32)
-            hot |= 1u << p;
-        const uint64_t ex = block_exclusive_scan_256_u64(v, warp_sums);
-        if (tid < RADIX) a.bins[p * RADIX + tid] = ex;
+    // Every pass at once: thread t takes bin base + t, so each group of 8
+    // warps holds one pass's 256 digits and scans them (a warp scan, then
+    // the sums of the group's earlier warps).  One round for up to 4
+    // passes, two for 8.
+    static_assert(HIST_THREADS % RADIX == 0, "whole passes per round");
+    __shared__ uint64_t wsum[HIST_THREADS / 32];
+    __shared__ uint32_t hot;  // bit p: pass p is hot
+    if (tid == 0) hot = 0;
+    __syncthreads();
+    const uint32_t warp = tid >> 5, total = a.passes * RADIX;
+    for (uint32_t base = 0; base < total; base += HIST_THREADS) {
+        const uint32_t i = base + tid, p = i / RADIX;
+        const uint64_t v = i < total ? __ldcg(&a.bins[i]) : 0;
+        if (i < total && v != a.n && v * HOT_SHARE >= a.n && p < 32) atomicOr(&hot, 1u << p);
+        uint64_t inc = v;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const uint64_t y = __shfl_up_sync(0xffffffffu, inc, off);
+            if (lane >= uint32_t(off)) inc += y;
+        }
+        if (lane == 31) wsum[warp] = inc;
+        __syncthreads();
+        uint64_t before = 0;
+        for (uint32_t w = warp & ~uint32_t(RADIX / 32 - 1); w < warp; ++w) before += wsum[w];
+        if (i < total) a.bins[i] = before + inc - v;
+        __syncthreads();  // wsum is rewritten by the next round
     }
     if (a.hot && tid == 0) *a.hot = int(hot);
 }
