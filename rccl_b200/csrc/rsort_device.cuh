@@ -433,11 +433,7 @@ __device__ __forceinline__ void warp_rank_items(DigitAt digit_at, uint32_t (&ran
         for (int u = 0; u < G; ++u)
             if (g + u < ITEMS) {
                 d[u] = digit_at(g + u);
-#ifdef RSORT_RANK_MATCH_ANY
-                peers[u] = __match_any_sync(0xffffffffu, d[u]);
-#else
                 peers[u] = match_digit(d[u], partial);
-#endif
             }
 #pragma unroll
         for (int u = 0; u < G; ++u) {

@@ -459,12 +459,8 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
         auto digit_at = [&](int j) {
             return live(j) ? digit_k<KIND>(key[j], a.shift, a.mask) : INVALID_DIGIT;
         };
-#ifdef RSORT_RANK_BALLOT
-        warp_rank_items<ITEMS>(digit_at, rank, whist + warp * RADIX, !FULL);
-#else
         warp_rank_items_or3<ITEMS, FULL, MODE>(digit_at, rank, whist + warp * WHIST_WORDS,
                                                wmask + warp * RANK_MASK_SETS * RADIX);
-#endif
         __syncthreads();
         const int64_t next = PERSIST ? int64_t(ctl[2]) : tiles;
 
@@ -497,13 +493,8 @@ __global__ void __launch_bounds__(ONESWEEP_THREADS, RSORT_MIN_BLOCKS) onesweep_k
 #pragma unroll
         for (int j = 0; j < ITEMS; ++j) {
             if (live(j)) {
-#ifndef RSORT_RANK_BALLOT
                 const uint32_t d = rank[j] >> 16;
                 const uint32_t rj = rank[j] & 0xffffu;
-#else
-                const uint32_t d = digit_k<KIND>(key[j], a.shift, a.mask);
-                const uint32_t rj = rank[j];
-#endif
                 const uint32_t r = whist[warp * RADIX + d] + rj;
                 if (r < count) {
                     skey[r] = key[j];
