@@ -61,6 +61,8 @@ template <typename B> struct HistShape {
     // shared by lane l of the CTA's 32 warps, and each key adds one to one
     // counter of every pass, so a counter stays at most 32 * FLUSH_KEYS.
     static constexpr uint32_t FLUSH_KEYS = 65535 / (HIST_THREADS / 32);
+    static_assert(uint64_t(FLUSH_KEYS) * (HIST_THREADS / 32) <= 0xffffu,
+                  "a 16-bit counter stays below 2^16 between flushes");
 };
 
 // Counts one key into every pass's digit counters (column already applied to
@@ -198,6 +200,11 @@ __global__ void __launch_bounds__(HIST_THREADS, 1) histogram_kernel(HistArgs a) 
             // One iteration of a thread counts HIST_UNROLL * PER keys from the
             // grid's step-aligned block of `step` vectors, so a chunk of whole
             // blocks holds every load its iterations issue.
+            // A chunk's iterations count at most FLUSH_KEYS - (PER - 1) keys
+            // per thread, leaving room for the scalar loop's last keys.
+            static_assert((S::FLUSH_KEYS / (HIST_UNROLL * PER)) * HIST_UNROLL * PER + PER - 1 <=
+                              S::FLUSH_KEYS,
+                          "vector chunk within the flush bound");
             const uint64_t chunk = step * (S::FLUSH_KEYS / (HIST_UNROLL * PER));
             for (uint64_t c0 = 0; c0 < nvec; c0 += chunk) {
                 const uint64_t c1 = nvec - c0 < chunk ? nvec : c0 + chunk;
