@@ -623,19 +623,18 @@ class SingleRun:
         L = _lib.lib()
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
         stops = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-        L.rsort_profile_read(None, None, 0)
-        L.rsort_profile_enable(1)
-        for _ in range(steps):
-            self.restore()
-            self.sort()
-        L.rsort_profile_enable(0)
-        torch.cuda.synchronize()
-        per_kernel = read_profile(L, 64 * steps)
-        L.rsort_launch_count_reset()
         sampler = (ClockSampler(torch.cuda.current_device()) if sample_clocks
                    else contextlib.nullcontext())
-        with sampler as clocks:
+        with sampler as clocks:  # both loops: the clocks cover the kernel times too
+            L.rsort_profile_read(None, None, 0)
+            L.rsort_profile_enable(1)
+            for _ in range(steps):
+                self.restore()
+                self.sort()
+            L.rsort_profile_enable(0)
             torch.cuda.synchronize()
+            per_kernel = read_profile(L, 64 * steps)
+            L.rsort_launch_count_reset()
             for i in range(steps):
                 self.restore()
                 starts[i].record(self.stream)
